@@ -1,0 +1,400 @@
+#!/usr/bin/env python3
+"""Benchmark of the SpMV hot path on B200: one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline workload: fp64 SpMV y = A x on the uniform-random matrix
+(1,000,000 x 1,000,000, exactly 16 distinct sorted uniform columns per row,
+values and x U(-1,1), seeded). A step is one SpMV over one such matrix with
+inputs resident in HBM. At N GPUs every rank runs its own matrix of that
+size (rank r's rows of an N*1M x 1M matrix, same x): weak scaling, no
+collective on the data path; `value` is the whole job's GFLOP/s (2*nnz per
+matrix). The kernel is the one the B200 heuristic picks for the matrix.
+
+Extra objects on the same line:
+  roofline      HBM roofline of the SpMV kernel (algorithmic bytes per launch
+                / CUDA-event launch time, over MEASURED_PEAKS.json hbm_gbs)
+  cpu_baseline  the reference's own csr_omp (oracle/_ref, compiled from the
+                reference sources; the C restatement if that is absent) on
+                the same matrix, all host threads, rank 0 at N=1
+  e2e           the same metric through spmvb_spmv_host (pinned host x in,
+                host y out, copies inside the timed region)
+  spmm_k64      fp64 SpMM Y = A X, X 1,000,000 x 64, same matrix, per-rank
+  iterated      x <- A x on ONE uniform matrix row-sharded over the N ranks
+                (nnz-balanced), x slices exchanged by ncclAllGather each step
+  clocks        nvidia-smi samples taken while the timed loop and a short
+                untimed run of the same kernel just before it execute
+
+--impl reference times the reference's CPU implementation (csr_omp) of the
+same workload on the host cores (rank 0 only) and prints the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOAD = "uniform_1m_16_fp64"
+METRIC = "fp64 SpMV GFLOP/s (uniform 1M x 1M, 16 nnz/row)"
+SEED = 2024
+X_SEED = 999
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--soak-s", type=float, default=1.5, help="untimed run before the timed loop (clock sampling)")
+    return p.parse_args()
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def spmv_bytes(m, n, nnz, vbytes=8, ibytes=4, ybytes=8):
+    """Compulsory traffic of CSR SpMV: values + colind + rowptr + x + y once
+    (the reference's bw_lo model, bench/bench_main.cpp:449-457)."""
+    return nnz * (vbytes + ibytes) + (m + 1) * ibytes + n * vbytes + m * ybytes
+
+
+def measured_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profiled_traffic(kernel_name: str):
+    """DRAM bytes per launch of `kernel_name` on this workload from the
+    committed ncu summary (profiles/*.md line `dram_bytes_per_launch: N`)."""
+    pdir = os.path.join(ROOT, "profiles")
+    if not os.path.isdir(pdir):
+        return None
+    for fn in sorted(os.listdir(pdir)):
+        if fn.startswith(kernel_name) and WORKLOAD in fn and fn.endswith(".md"):
+            m = re.search(r"dram_bytes_per_launch:\s*([0-9]+)", open(os.path.join(pdir, fn)).read())
+            if m:
+                return int(m.group(1))
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples every 200 ms (read only)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = gpus
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", ",".join(str(g) for g in self.gpus), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [c.strip() for c in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        loaded = [s for s in sm if mx and s > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------
+def cpu_reference_time(A, x, min_runs=10, budget_s=10.0, threads=None):
+    """csr_omp on the host: 3 warm-up runs, then runs until `budget_s` (at
+    least `min_runs`); median ms. The reference's own code when oracle/_ref
+    was built, else the C restatement."""
+    import oracle
+    threads = threads or host_threads()
+    if oracle.ref_available():
+        R = oracle.RefCsr(A.m, A.n, A.rowptr, A.colind, A.values)
+        y = np.empty(A.m)
+        run = lambda: R.spmv(x, np.float64, threads, out=y)  # noqa: E731
+        kind = "reference"
+    else:
+        run = lambda: oracle.spmv_csr(A.m, A.rowptr, A.colind, A.values, x, np.float64, threads)  # noqa: E731
+        kind = "port"
+    for _ in range(3):
+        run()
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < min_runs or (time.perf_counter() < t_end and len(times) < 500):
+        t0 = time.perf_counter()
+        run()
+        times.append((time.perf_counter() - t0) * 1e3)
+    return statistics.median(times), len(times), kind, threads
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import spmvbench_b200 as S
+    A = S.generate(2, seed=SEED)
+    x = S.generate_vector(X_SEED, A.n)
+    import oracle
+    threads = host_threads()
+    if oracle.ref_available():
+        R = oracle.RefCsr(A.m, A.n, A.rowptr, A.colind, A.values)
+        y = np.empty(A.m)
+        run = lambda: R.spmv(x, np.float64, threads, out=y)  # noqa: E731
+        kind = "reference"
+    else:
+        run = lambda: oracle.spmv_csr(A.m, A.rowptr, A.colind, A.values, x, np.float64, threads)  # noqa: E731
+        kind = "port"
+    for _ in range(args.warmup):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        run()
+    ms = (time.perf_counter() - t0) * 1e3 / args.steps
+    gflops = 2.0 * A.nnz / (ms * 1e-3) / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": gflops, "unit": "GFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "m": A.m, "n": A.n, "nnz": A.nnz,
+                   "kernel": "csr_omp (spmv_csr_cpu, OpenMP static)"},
+        "cpu_baseline": {"value": gflops, "unit": "GFLOP/s", "cores": threads, "kind": kind,
+                         "sample": f"full {WORKLOAD} SpMV per step, {args.steps} steps after {args.warmup} warm-up"},
+        "e2e": {"value": gflops, "unit": "GFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+
+    import torch
+    import torch.distributed as dist
+
+    import spmvbench_b200 as S
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ctx = S.Context(local)
+    stream = torch.cuda.current_stream()
+
+    # ---- workload: this rank's uniform 1M x 1M matrix, fp64 ----
+    A = S.generate(2, seed=SEED + rank)
+    xh = S.generate_vector(X_SEED, A.n)
+    stats = S.row_stats(A)
+    choice = S.choose_spmv(stats)
+    kernel, lanes, block = choice["kernel"], choice["lanes"], choice["block_r"]
+    M = S.DeviceMatrix(ctx, A, S.F64)
+    M.prepare(kernel, block if kernel == S.BCSR else 0)
+    x = torch.from_numpy(xh).cuda()
+    y = torch.empty(A.m, dtype=torch.float64, device="cuda")
+
+    def step():
+        M.spmv(x, y, kernel=kernel, lanes=lanes, block=block, stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    sampler = ClockSampler(list(range(world)) if rank == 0 else [])
+    if rank == 0:
+        sampler.start()
+    t_soak = time.perf_counter() + args.soak_s
+    while time.perf_counter() < t_soak:  # untimed, same kernel, keeps clocks at their loaded state
+        for _ in range(20):
+            step()
+        torch.cuda.synchronize()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = S.launch_count()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    ev1.synchronize()
+    launches = S.launch_count() - launches0
+    barrier()
+    clocks = sampler.stop() if rank == 0 else None
+    ms_rank = ev0.elapsed_time(ev1) / args.steps
+    ms = max_over_ranks(ms_rank)
+    gflops = world * 2.0 * A.nnz / (ms * 1e-3) / 1e9
+
+    bytes_launch = spmv_bytes(A.m, A.n, A.nnz)
+    peak, peak_src = measured_peak()
+    achieved = bytes_launch / (ms * 1e-3) / 1e9
+    kname = {S.CSR_SCALAR: "csr_scalar_staged", S.CSR_MERGE: "csr_merge", S.CSR_VECTOR: "csr_vector",
+             S.CSR_WARP: "csr_vector", S.ELL: "ell_rows", S.HYB: "ell_rows", S.BCSR: "bcsr_rows"}[kernel]
+
+    # parity spot check of this rank's result (host reference from the oracle is
+    # not used here; the kernel's own contract is tested in tests/)
+    # ---- e2e through the host-buffer entry point ----
+    xp = torch.from_numpy(xh.copy()).pin_memory()
+    yp = torch.empty(A.m, dtype=torch.float64).pin_memory()
+    xp_np, yp_np = xp.numpy(), yp.numpy()
+    for _ in range(3):
+        M.spmv_host(xp_np, kernel=kernel, lanes=lanes, block=block, out=yp_np, stream=stream)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        M.spmv_host(xp_np, kernel=kernel, lanes=lanes, block=block, out=yp_np, stream=stream)
+    e1.record(stream)
+    e1.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    e2e = {"value": world * 2.0 * A.nnz / (e2e_ms * 1e-3) / 1e9, "unit": "GFLOP/s",
+           "ms_per_step": e2e_ms, "h2d_bytes_per_step": int(A.n * 8), "d2h_bytes_per_step": int(A.m * 8)}
+
+    # ---- SpMM k=64 on the same matrix ----
+    k = 64
+    Xd = torch.from_numpy(S.generate_vector(X_SEED + 1, A.n * k).reshape(A.n, k)).cuda()
+    Yd = torch.empty(A.m, k, dtype=torch.float64, device="cuda")
+    for _ in range(args.warmup):
+        M.spmm(Xd, Yd, k, tile=64, stream=stream)
+    barrier()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    spmm_steps = max(3, args.steps // 5)
+    s0.record(stream)
+    for _ in range(spmm_steps):
+        M.spmm(Xd, Yd, k, tile=64, stream=stream)
+    s1.record(stream)
+    s1.synchronize()
+    barrier()
+    spmm_ms = max_over_ranks(s0.elapsed_time(s1) / spmm_steps)
+    spmm_bytes = A.nnz * 12 + (A.m + 1) * 4 + A.n * k * 8 + A.m * k * 8
+    spmm = {"value": world * 2.0 * A.nnz * k / (spmm_ms * 1e-3) / 1e9, "unit": "GFLOP/s", "k": k, "tile": 64,
+            "ms_per_step": spmm_ms, "steps": spmm_steps,
+            "compulsory_gbs": spmm_bytes / (spmm_ms * 1e-3) / 1e9,
+            "no_reuse_gbs": (A.nnz * 12 + (A.m + 1) * 4 + A.nnz * k * 8 + A.m * k * 8) / (spmm_ms * 1e-3) / 1e9}
+    del Xd, Yd
+
+    # ---- iterated y = A x, x <- y, one matrix row-sharded over the ranks ----
+    A0 = A if rank == 0 else S.generate(2, seed=SEED)
+    bounds = S.partition_rows(A0.rowptr, world)
+    uid = None
+    if world > 1:
+        obj = [S.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        uid = obj[0]
+    D = S.DistMatrix(ctx, world, rank, uid, A0, bounds, S.F64)
+    D.set_x(xh / 4.0)
+    D.iterate(args.warmup, kernel=kernel, lanes=lanes, stream=stream)
+    barrier()
+    it_steps = args.steps
+    kms, sms = D.iterate_timed(it_steps, kernel=kernel, lanes=lanes, stream=stream)
+    barrier()
+    it_ms = max_over_ranks(sms / it_steps)
+    it_kms = max_over_ranks(kms / it_steps)
+    iterated = {"value": 2.0 * A0.nnz / (it_ms * 1e-3) / 1e9, "unit": "GFLOP/s", "ms_per_step": it_ms,
+                "kernel_ms_per_step": it_kms, "exchange": "ncclAllGather" if world > 1 else "none",
+                "bounds": bounds.tolist(), "scaling": "strong"}
+    D.close()
+
+    # ---- CPU baseline (rank 0, N = 1 only) ----
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cms, runs, kind, threads = cpu_reference_time(A, xh)
+        cpu = {"value": 2.0 * A.nnz / (cms * 1e-3) / 1e9, "unit": "GFLOP/s", "cores": threads, "kind": kind,
+               "sample": f"full {WORKLOAD} csr_omp SpMV, median of {runs} runs after 3 warm-up"}
+
+    if rank == 0:
+        traffic = profiled_traffic(kname)
+        line = {
+            "metric": METRIC, "value": gflops, "unit": "GFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "m": A.m, "n": A.n, "nnz": A.nnz, "per_rank": True,
+                       "kernel": S.kernel_name(kernel), "lanes": lanes, "rule": choice["reason"],
+                       "bytes_per_step": bytes_launch,
+                       "l2": "inputs larger than L2 (212 MB per step vs 126 MB), no flush"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_source": peak_src,
+                         "traffic": traffic, "kernel": kname},
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks,
+            "spmm_k64": spmm, "iterated": iterated,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,303 @@
+/*
+ * spmvb.h - C ABI of the B200 (sm_100a) sparse kernel library.
+ *
+ * This is the drop-in boundary for SpMVBench's `src/cuda` path. Every entry
+ * point takes plain pointers and sizes and returns a status code instead of
+ * aborting. The comment above each declaration names the reference interface
+ * it replaces (paths relative to the SpMVBench source tree).
+ *
+ * Conventions
+ *  - Index type is int32 (reference `Index`, include/spmvbench/dtypes.hpp:19).
+ *  - Value type `dtype` is the storage type T of the matrix and of x / X;
+ *    `acc` is the accumulator / output type Acc of y / Y. Supported (T, Acc):
+ *    (F32, F32), (F32, F64), (F64, F64) - the instantiations of
+ *    src/cuda/spmv_cuda.cu:503-505.
+ *  - Pointers named d_* are device pointers, h_* host pointers.
+ *  - `stream` is a cudaStream_t passed as void*; NULL is the legacy default
+ *    stream, as in the reference.
+ *  - A matrix handle may be used by one stream at a time (its lazily built
+ *    formats and its merge-path carry buffer are per handle).
+ *  - spmvb_last_error() returns a thread-local message for the last failing
+ *    call made on this host thread.
+ */
+#ifndef SPMVB_H
+#define SPMVB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SPMVB_ABI_VERSION 1
+
+typedef enum spmvb_status {
+  SPMVB_OK = 0,
+  SPMVB_ERR_INVALID_ARGUMENT = 1, /* bad pointer, size, kernel id, dtype  */
+  SPMVB_ERR_INVALID_MATRIX = 2,   /* rowptr/colind fail validation         */
+  SPMVB_ERR_UNSUPPORTED = 3,      /* valid request this build cannot serve */
+  SPMVB_ERR_OUT_OF_MEMORY = 4,    /* device or host allocation failed      */
+  SPMVB_ERR_CUDA = 5,             /* CUDA runtime error (message attached) */
+  SPMVB_ERR_NCCL = 6,             /* NCCL error (message attached)         */
+  SPMVB_ERR_TIMEOUT = 7,          /* a bounded wait gave up                */
+  SPMVB_ERR_NO_DEVICE = 8         /* no CUDA device / bad device ordinal   */
+} spmvb_status;
+
+typedef enum spmvb_dtype { SPMVB_F32 = 0, SPMVB_F64 = 1 } spmvb_dtype;
+
+/* SpMV kernels. 0..5 keep the numeric values of the reference's KernelId
+ * (include/spmvbench/select.hpp:11-19); SPMVB_HYB is new (hybrid ELL+CSR). */
+typedef enum spmvb_kernel {
+  SPMVB_CSR_SCALAR = 0, /* one row per thread, csr_omp summation order      */
+  SPMVB_CSR_VECTOR = 1, /* `lanes` lanes per row (2,4,8,16,32)               */
+  SPMVB_CSR_WARP = 2,   /* one warp per row                                  */
+  SPMVB_CSR_MERGE = 3,  /* merge-path: equal (rows + nnz) share per thread   */
+  SPMVB_ELL = 4,        /* column-major ELL, walks row_lengths               */
+  SPMVB_BCSR = 5,       /* blocked CSR, `block` = 2 (2x2) or 4 (4x4)         */
+  SPMVB_HYB = 6,        /* ELL(K) for the first K entries + CSR tail         */
+  SPMVB_KERNEL_COUNT = 7
+} spmvb_kernel;
+
+typedef struct spmvb_context_st* spmvb_context;
+typedef struct spmvb_matrix_st* spmvb_matrix;
+typedef struct spmvb_dist_st* spmvb_dist;
+
+/* Device description. Replaces GpuInfo / query_gpu()
+ * (include/spmvbench/spmv_cuda.cuh:101-111, src/cuda/spmv_cuda.cu:197-228);
+ * peak_gbs is the theoretical HBM figure (2 x memory clock x bus width). */
+typedef struct spmvb_gpu_info {
+  char name[256];
+  int major;
+  int minor;
+  int sm_count;
+  int l2_bytes;
+  int max_smem_per_block;
+  int64_t global_mem_bytes;
+  double peak_gbs;
+  int peak_known;
+} spmvb_gpu_info;
+
+/* Storage sizes of the formats a matrix handle holds. Replaces
+ * SpmvRunner::ell_padded_nnz / ell_touched_nnz / bcsr_block_nnz
+ * (include/spmvbench/spmv_cuda.cuh:137-140). -1 = not built yet. */
+typedef struct spmvb_matrix_info {
+  int32_t m;
+  int32_t n;
+  int64_t nnz;
+  spmvb_dtype dtype;
+  int32_t max_row_nnz;
+  int64_t ell_padded_nnz;  /* m * max_row_nnz                               */
+  int64_t ell_touched_nnz; /* entries the ELL kernel reads (= nnz)           */
+  int64_t bcsr2_block_nnz;
+  int64_t bcsr4_block_nnz;
+  int32_t hyb_width;       /* K of the hybrid format                        */
+  int64_t hyb_ell_nnz;     /* entries held in the ELL(K) part               */
+  int64_t hyb_tail_nnz;    /* entries held in the CSR tail                  */
+  int32_t hyb_long_rows;   /* rows whose length exceeds K                   */
+  int64_t device_bytes;    /* device memory owned by the handle             */
+} spmvb_matrix_info;
+
+/* Row statistics. Same fields and definitions as RowStats
+ * (include/spmvbench/stats.hpp:14-40, src/stats.cpp:13-123). */
+typedef struct spmvb_row_stats {
+  int64_t nnz;
+  int32_t rows;
+  int32_t cols;
+  double mean_row_nnz;
+  double median_row_nnz;
+  int32_t min_row_nnz;
+  int32_t max_row_nnz;
+  double stddev_row_nnz;
+  double cv_row_nnz;
+  double max_over_mean;
+  double ell_padding_overhead;
+  double frac_dense_blocks_4x4;
+  double density;
+  /* Not in the reference: dense 4x4 blocks (> 8 entries) over the 4x4
+   * blocks that hold at least one entry. frac_dense_blocks_4x4 divides by
+   * every possible block (mb*nb), so it stays near 0 for any large sparse
+   * matrix, however blocky. */
+  double dense_share_of_stored_4x4;
+} spmvb_row_stats;
+
+/* Kernel choice. Same fields as KernelChoice (include/spmvbench/select.hpp:21-27). */
+typedef struct spmvb_choice {
+  int32_t kernel; /* spmvb_kernel */
+  int32_t lanes;
+  int32_t block_r;
+  int32_t block_c;
+  int32_t rule;   /* index of the rule that fired                           */
+  char reason[256];
+} spmvb_choice;
+
+/* ---- library / device -------------------------------------------------- */
+const char* spmvb_version(void);
+const char* spmvb_last_error(void);
+const char* spmvb_status_string(spmvb_status s);
+/* Kernel launches issued by this library since load (all devices). */
+uint64_t spmvb_launch_count(void);
+
+/* Replaces gpu_available() (include/spmvbench/spmv_cuda.cuh:110): never aborts. */
+int spmvb_gpu_available(void);
+/* Replaces query_gpu() (include/spmvbench/spmv_cuda.cuh:111). */
+spmvb_status spmvb_query_gpu(int device, spmvb_gpu_info* out);
+
+/* A context binds one device. Replaces the implicit current-device state the
+ * reference's SpmvRunner relies on (src/cuda/spmv_cuda.cu:233-290). */
+spmvb_status spmvb_context_create(int device, spmvb_context* out);
+spmvb_status spmvb_context_destroy(spmvb_context ctx);
+
+/* ---- matrices ------------------------------------------------------------ */
+/* Validate a host CSR (rowptr[0]==0, non-decreasing, rowptr[m]==nnz, every
+ * column in [0,n)) and upload it. Replaces SpmvRunner(const CsrMatrix<T>&)
+ * and its upload_matrix (src/cuda/spmv_cuda.cu:233-290); other formats are
+ * built lazily by spmvb_matrix_prepare or on first use. Columns inside a row
+ * may be unsorted, as csr.hpp:13-15 allows. */
+spmvb_status spmvb_matrix_create_csr(spmvb_context ctx, spmvb_dtype dtype,
+                                     int32_t m, int32_t n, int64_t nnz,
+                                     const int32_t* h_rowptr,
+                                     const int32_t* h_colind,
+                                     const void* h_values, spmvb_matrix* out);
+spmvb_status spmvb_matrix_destroy(spmvb_matrix A);
+/* The host-side validation spmvb_matrix_create_csr applies, on its own (no
+ * device needed). *max_row_nnz (optional) receives the longest row. */
+spmvb_status spmvb_csr_validate(int32_t m, int32_t n, int64_t nnz,
+                                const int32_t* h_rowptr,
+                                const int32_t* h_colind,
+                                int32_t* max_row_nnz);
+/* Build what `kernel` needs (ELL, HYB, BCSR `block`, merge-path partition)
+ * ahead of the first call; kernel = -1 builds the SpMM row-length buckets.
+ * param: block size for SPMVB_BCSR, forced width K for SPMVB_HYB
+ * (0 = automatic). Lazy builds synchronize the device, so call this before
+ * capturing a stream into a CUDA graph. */
+spmvb_status spmvb_matrix_prepare(spmvb_matrix A, spmvb_kernel kernel,
+                                  int param);
+spmvb_status spmvb_matrix_get_info(spmvb_matrix A, spmvb_matrix_info* out);
+
+/* Download a device-built format in the reference host layout, for
+ * bit-exact comparison with csr_to_ell (src/formats.cpp:14-43): colind and
+ * values column-major, size m*max_row_nnz, padding column 0 / value 0. */
+spmvb_status spmvb_matrix_export_ell(spmvb_matrix A, int32_t* h_colind,
+                                     void* h_values, int32_t* h_row_lengths);
+/* Same for csr_to_bcsr<T,R,C> (src/formats.cpp:45-105), R=C=block:
+ * rowptr (mb+1), block colind (block_nnz), values (block_nnz*block*block). */
+spmvb_status spmvb_matrix_export_bcsr(spmvb_matrix A, int block,
+                                      int32_t* h_rowptr, int32_t* h_colind,
+                                      void* h_values);
+
+/* ---- SpMV ------------------------------------------------------------------ */
+/* y = A x on device buffers. x has n entries of the matrix dtype, y has m
+ * entries of `acc`. `lanes` applies to SPMVB_CSR_VECTOR, `block` to
+ * SPMVB_BCSR, with the reference's defaults and clamping
+ * (src/cuda/spmv_cuda.cu:392-458). Replaces the launch inside
+ * SpmvRunner::run (src/cuda/spmv_cuda.cu:376-464). */
+spmvb_status spmvb_spmv(spmvb_matrix A, spmvb_kernel kernel, int lanes,
+                        int block, const void* d_x, void* d_y,
+                        spmvb_dtype acc, void* stream);
+/* Same on host buffers: H2D of x, the kernel and D2H of y in stream order,
+ * synchronous on return. Replaces set_x + run + result
+ * (include/spmvbench/spmv_cuda.cuh:127-135). */
+spmvb_status spmvb_spmv_host(spmvb_matrix A, spmvb_kernel kernel, int lanes,
+                             int block, const void* h_x, void* h_y,
+                             spmvb_dtype acc, void* stream);
+
+/* ---- SpMM ------------------------------------------------------------------ */
+/* Y (m x k, row-major, acc) = A X (n x k, row-major, matrix dtype).
+ * tile in {16,32,64}: columns of Y a row group covers per pass; bucketed != 0
+ * selects the row-length-bucketed variant (buckets built once per handle).
+ * Replaces the kernels behind spmm_csr_tiled_f32/f64
+ * (include/spmvbench/spmm_cuda.cuh:34-41, src/cuda/spmm_cuda.cu:151-212). */
+spmvb_status spmvb_spmm(spmvb_matrix A, int tile, int bucketed, int k,
+                        const void* d_X, void* d_Y, spmvb_dtype acc,
+                        void* stream);
+/* Host-buffer form (H2D X, kernel, D2H Y). Replaces run_tiled's data path
+ * (src/cuda/spmm_cuda.cu:214-325) without its per-call malloc/free. */
+spmvb_status spmvb_spmm_host(spmvb_matrix A, int tile, int bucketed, int k,
+                             const void* h_X, void* h_Y, spmvb_dtype acc,
+                             void* stream);
+
+/* ---- statistics and kernel selection ---------------------------------------- */
+/* Replaces compute_row_stats (include/spmvbench/stats.hpp:44-52). histogram
+ * (optional) receives max_row_nnz+1 counts when hist_cap is large enough;
+ * the dense-block scan is hashed, O(nnz) instead of O(L^2) per block row. */
+spmvb_status spmvb_compute_row_stats(const int32_t* h_rowptr, const int32_t* h_colind,
+                             int32_t m, int32_t n, int64_t nnz,
+                             spmvb_row_stats* out, int64_t* h_histogram,
+                             int64_t hist_cap);
+/* Replaces choose_spmv (include/spmvbench/select.hpp:33) with rules
+ * calibrated on B200 measurements. */
+spmvb_status spmvb_choose_spmv(const spmvb_row_stats* stats,
+                               spmvb_choice* out);
+/* The reference's own rule set, unchanged (src/select.cpp:93-165). */
+spmvb_status spmvb_choose_spmv_reference(const spmvb_row_stats* stats,
+                                         spmvb_choice* out);
+/* Replaces kernel_name (src/select.cpp:73-91); adds "hyb". */
+const char* spmvb_kernel_name(int kernel);
+
+/* ---- synthetic inputs ------------------------------------------------------ */
+/* Seeded generators for the five benchmark matrices (no reference
+ * counterpart; the reference reads .mtx files). `which`: 1 banded 100k hb=4,
+ * 2 uniform 1M x 16, 3 power-law Zipf(2.1) <= 50,000, 4 dense-4x4-block 500k,
+ * 5 = 2 (the SpMM operand). `scale_rows` (0 = full size) shrinks m for tests.
+ * Two calls: with h_colind == NULL the sizes are returned in *m,*n,*nnz;
+ * then the caller allocates and calls again. Values are f64. */
+spmvb_status spmvb_generate(int which, uint64_t seed, int32_t scale_rows,
+                            int32_t* m, int32_t* n, int64_t* nnz,
+                            int32_t* h_rowptr, int32_t* h_colind,
+                            double* h_values);
+/* x_i ~ U(-1,1) from a seeded 64-bit generator, shared by oracle and GPU. */
+spmvb_status spmvb_generate_vector(uint64_t seed, int64_t len, double* h_out);
+
+/* ---- multi-GPU row sharding ---------------------------------------------------- */
+/* nnz-balanced contiguous row blocks: bounds[g] = lower_bound(rowptr,
+ * ceil(g*nnz/parts)) for g in 1..parts-1, bounds[0]=0, bounds[parts]=m. */
+spmvb_status spmvb_partition_rows(const int32_t* h_rowptr, int32_t m,
+                                  int32_t parts, int32_t* h_bounds);
+/* Host-only shard planning used by spmvb_dist_create: rank `rank`'s rows
+ * [bounds[rank], bounds[rank+1]) of a square m x m CSR with every column c
+ * renumbered to its padded gather slot owner(c)*max_rows + (c -
+ * bounds[owner(c)]), max_rows = the largest part. With h_out_colind == NULL
+ * only *max_rows and *local_nnz are returned. h_out_rowptr has
+ * local_rows+1 entries. */
+spmvb_status spmvb_shard_csr(int32_t m, const int32_t* h_rowptr,
+                             const int32_t* h_colind, int nranks, int rank,
+                             const int32_t* h_bounds, int32_t* max_rows,
+                             int64_t* local_nnz, int32_t* h_out_rowptr,
+                             int32_t* h_out_colind);
+/* NCCL unique id (NCCL_UNIQUE_ID_BYTES = 128) created on one rank and
+ * broadcast by the caller. */
+spmvb_status spmvb_nccl_unique_id(void* h_out, size_t cap);
+/* One rank's shard of a square row-partitioned matrix for iterated y = A x
+ * with x <- y. The caller passes the global rowptr/colind/values (host) and
+ * the bounds from spmvb_partition_rows; the shard's columns are renumbered
+ * into the padded gather layout once (slot = owner*max_rows + local). */
+spmvb_status spmvb_dist_create(spmvb_context ctx, int nranks, int rank,
+                               const void* h_unique_id, spmvb_dtype dtype,
+                               int32_t m, int64_t nnz,
+                               const int32_t* h_rowptr,
+                               const int32_t* h_colind, const void* h_values,
+                               const int32_t* h_bounds, spmvb_dist* out);
+spmvb_status spmvb_dist_destroy(spmvb_dist D);
+/* Load the global x (host, m entries) into this rank's padded x buffer. */
+spmvb_status spmvb_dist_set_x(spmvb_dist D, const void* h_x, void* stream);
+/* `iters` steps of: y_local = A_local x (kernel), then ncclAllGather of the
+ * padded y slices into x. The final x (global, m entries) can be read back
+ * with spmvb_dist_get_x. */
+spmvb_status spmvb_dist_iterate(spmvb_dist D, spmvb_kernel kernel, int lanes,
+                                int iters, void* stream);
+/* Same, timing only the local SpMV of each step on device events; returns
+ * per-step kernel milliseconds summed over the steps in *kernel_ms. */
+spmvb_status spmvb_dist_iterate_timed(spmvb_dist D, spmvb_kernel kernel,
+                                      int lanes, int iters, void* stream,
+                                      double* kernel_ms, double* step_ms);
+spmvb_status spmvb_dist_get_x(spmvb_dist D, void* h_x, void* stream);
+spmvb_status spmvb_dist_get_info(spmvb_dist D, int32_t* row_begin,
+                                 int32_t* row_end, int32_t* max_rows,
+                                 int64_t* local_nnz);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPMVB_H */

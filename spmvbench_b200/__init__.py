@@ -1,0 +1,342 @@
+"""spmvbench_b200 - B200 (sm_100a) SpMV / SpMM kernels behind the C ABI of
+include/spmvb.h, with a thin Python mirror used by the tests and bench.py.
+
+The Python layer only moves arguments: every computation runs in
+lib/libspmvb.so (hand-written CUDA kernels plus the C++ host runtime).
+Device buffers are torch tensors (torch is used for device memory and
+streams only). Host-side matrices are numpy CSR triples, mirroring the
+reference's CsrMatrix<T> (include/spmvbench/csr.hpp:16-35).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib
+from ._lib import (BCSR, CSR_MERGE, CSR_SCALAR, CSR_VECTOR, CSR_WARP, ELL, F32, F64, HYB,
+                   KERNEL_NAMES, SpmvbError, call, load)
+
+__all__ = [
+    "CsrMatrix", "Context", "DeviceMatrix", "DistMatrix", "SpmvbError", "generate",
+    "generate_vector", "row_stats", "choose_spmv", "choose_spmv_reference", "partition_rows",
+    "launch_count", "gpu_available", "csr_validate", "shard_csr", "query_gpu", "kernel_name", "nccl_unique_id",
+    "CSR_SCALAR", "CSR_VECTOR", "CSR_WARP", "CSR_MERGE", "ELL", "BCSR", "HYB", "F32", "F64",
+    "KERNEL_NAMES", "WORKLOADS",
+]
+
+# Benchmark workloads produced by generate(): id -> name.
+WORKLOADS = {1: "banded_100k_hb4", 2: "uniform_1m_16", 3: "powerlaw_1m_zipf2.1",
+             4: "bcsr4x4_500k_8blk", 5: "spmm_uniform_1m_16_k64"}
+
+
+def _np_dtype(d: int):
+    return np.float64 if d == F64 else np.float32
+
+
+def _ptr(a: np.ndarray):
+    return a.ctypes.data_as(C.c_void_p) if a is not None and a.size else None
+
+
+@dataclass
+class CsrMatrix:
+    """Host CSR with int32 indices (reference CsrMatrix<T>)."""
+    m: int
+    n: int
+    rowptr: np.ndarray
+    colind: np.ndarray
+    values: np.ndarray
+
+    @property
+    def nnz(self) -> int:
+        return int(self.rowptr[self.m]) if self.m else 0
+
+    def astype(self, dtype) -> "CsrMatrix":
+        return CsrMatrix(self.m, self.n, self.rowptr, self.colind,
+                         np.ascontiguousarray(self.values, dtype=dtype))
+
+    def row_lengths(self) -> np.ndarray:
+        return np.diff(self.rowptr)
+
+
+def generate(which: int, seed: int = 2024, scale_rows: int = 0) -> CsrMatrix:
+    """Seeded benchmark matrix `which` (1..5, see WORKLOADS), fp64 values."""
+    lib = load()
+    m, n, nnz = C.c_int32(), C.c_int32(), C.c_int64()
+    _lib.check(lib.spmvb_generate(which, seed, scale_rows, C.byref(m), C.byref(n), C.byref(nnz),
+                                  None, None, None), "spmvb_generate")
+    rowptr = np.zeros(m.value + 1, np.int32)
+    colind = np.zeros(max(nnz.value, 1), np.int32)
+    values = np.zeros(max(nnz.value, 1), np.float64)
+    _lib.check(lib.spmvb_generate(which, seed, scale_rows, C.byref(m), C.byref(n), C.byref(nnz),
+                                  _ptr(rowptr), colind.ctypes.data_as(C.c_void_p),
+                                  values.ctypes.data_as(C.c_void_p)), "spmvb_generate")
+    return CsrMatrix(m.value, n.value, rowptr, colind[:nnz.value], values[:nnz.value])
+
+
+def generate_vector(seed: int, n: int) -> np.ndarray:
+    out = np.empty(n, np.float64)
+    call("spmvb_generate_vector", seed, n, _ptr(out))
+    return out
+
+
+def launch_count() -> int:
+    return int(load().spmvb_launch_count())
+
+
+def gpu_available() -> bool:
+    return bool(load().spmvb_gpu_available())
+
+
+def query_gpu(device: int = 0) -> dict:
+    g = _lib.GpuInfo()
+    call("spmvb_query_gpu", device, C.byref(g))
+    return {"name": g.name.decode(), "major": g.major, "minor": g.minor, "sm_count": g.sm_count,
+            "l2_bytes": g.l2_bytes, "global_mem_bytes": g.global_mem_bytes,
+            "peak_gbs": g.peak_gbs, "peak_known": bool(g.peak_known)}
+
+
+def kernel_name(k: int) -> str:
+    return load().spmvb_kernel_name(k).decode()
+
+
+def row_stats(A: CsrMatrix, histogram: bool = False) -> dict:
+    s = _lib.RowStats()
+    rp = np.ascontiguousarray(A.rowptr, np.int32)
+    ci = np.ascontiguousarray(A.colind, np.int32)
+    hist = None
+    if histogram:
+        mx = int(np.max(np.diff(rp))) if A.m else 0
+        hist = np.zeros(mx + 1, np.int64)
+    call("spmvb_compute_row_stats", _ptr(rp), _ptr(ci), A.m, A.n, A.nnz, C.byref(s),
+         _ptr(hist), 0 if hist is None else hist.size)
+    d = {f: getattr(s, f) for f, _ in _lib.RowStats._fields_}
+    if histogram:
+        d["row_nnz_histogram"] = hist
+    return d
+
+
+def _stats_struct(d: dict) -> _lib.RowStats:
+    s = _lib.RowStats()
+    for f, _ in _lib.RowStats._fields_:
+        setattr(s, f, d.get(f, 0))
+    return s
+
+
+def _choice(fn: str, stats: dict) -> dict:
+    c = _lib.Choice()
+    call(fn, C.byref(_stats_struct(stats)), C.byref(c))
+    return {"kernel": c.kernel, "lanes": c.lanes, "block_r": c.block_r, "block_c": c.block_c,
+            "rule": c.rule, "reason": c.reason.decode(), "name": kernel_name(c.kernel)}
+
+
+def choose_spmv(stats: dict) -> dict:
+    """B200 kernel choice from row statistics."""
+    return _choice("spmvb_choose_spmv", stats)
+
+
+def choose_spmv_reference(stats: dict) -> dict:
+    """The reference's rule set (src/select.cpp:93-165), unchanged."""
+    return _choice("spmvb_choose_spmv_reference", stats)
+
+
+def partition_rows(rowptr: np.ndarray, parts: int) -> np.ndarray:
+    rp = np.ascontiguousarray(rowptr, np.int32)
+    out = np.zeros(parts + 1, np.int32)
+    call("spmvb_partition_rows", _ptr(rp), rp.size - 1, parts, _ptr(out))
+    return out
+
+
+def csr_validate(A: CsrMatrix) -> int:
+    """Host validation of a CSR (raises SpmvbError); returns the longest row."""
+    rp = np.ascontiguousarray(A.rowptr, np.int32)
+    ci = np.ascontiguousarray(A.colind, np.int32)
+    mx = C.c_int32()
+    call("spmvb_csr_validate", A.m, A.n, A.nnz, _ptr(rp), _ptr(ci), C.byref(mx))
+    return mx.value
+
+
+def shard_csr(A: CsrMatrix, bounds: np.ndarray, rank: int):
+    """Rank `rank`'s rows of a square CSR with columns renumbered into the
+    padded gather layout. Returns (max_rows, local rowptr, local colind)."""
+    rp = np.ascontiguousarray(A.rowptr, np.int32)
+    ci = np.ascontiguousarray(A.colind, np.int32)
+    b = np.ascontiguousarray(bounds, np.int32)
+    nranks = b.size - 1
+    mr, ln = C.c_int32(), C.c_int64()
+    call("spmvb_shard_csr", A.m, _ptr(rp), _ptr(ci), nranks, rank, _ptr(b), C.byref(mr), C.byref(ln), None, None)
+    orp = np.zeros(int(b[rank + 1] - b[rank]) + 1, np.int32)
+    oci = np.zeros(max(ln.value, 1), np.int32)
+    call("spmvb_shard_csr", A.m, _ptr(rp), _ptr(ci), nranks, rank, _ptr(b), C.byref(mr), C.byref(ln),
+         _ptr(orp), oci.ctypes.data_as(C.c_void_p))
+    return mr.value, orp, oci[:ln.value]
+
+
+def nccl_unique_id() -> bytes:
+    buf = (C.c_char * 128)()
+    call("spmvb_nccl_unique_id", buf, 128)
+    return bytes(buf)
+
+
+def _stream_ptr(stream):
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return C.c_void_p(stream.cuda_stream)
+
+
+class Context:
+    """One device (spmvb_context)."""
+
+    def __init__(self, device: int = 0):
+        h = C.c_void_p()
+        call("spmvb_context_create", device, C.byref(h))
+        self.handle = h
+        self.device = device
+
+    def close(self):
+        if self.handle:
+            load().spmvb_context_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class DeviceMatrix:
+    """A matrix uploaded to one device (spmvb_matrix). `dtype` is the storage
+    type; kernels accept acc = dtype, or F64 accumulation of F32 storage."""
+
+    def __init__(self, ctx: Context, A: CsrMatrix, dtype: int = F64):
+        self.ctx = ctx
+        self.m, self.n, self.nnz = A.m, A.n, A.nnz
+        self.dtype = dtype
+        rp = np.ascontiguousarray(A.rowptr, np.int32)
+        ci = np.ascontiguousarray(A.colind, np.int32)
+        va = np.ascontiguousarray(A.values, _np_dtype(dtype))
+        h = C.c_void_p()
+        call("spmvb_matrix_create_csr", ctx.handle, dtype, A.m, A.n, A.nnz, _ptr(rp), _ptr(ci),
+             _ptr(va), C.byref(h))
+        self.handle = h
+
+    def close(self):
+        if getattr(self, "handle", None):
+            load().spmvb_matrix_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def prepare(self, kernel: int, param: int = 0) -> None:
+        call("spmvb_matrix_prepare", self.handle, kernel, param)
+
+    def info(self) -> dict:
+        i = _lib.MatrixInfo()
+        call("spmvb_matrix_get_info", self.handle, C.byref(i))
+        return {f: getattr(i, f) for f, _ in _lib.MatrixInfo._fields_}
+
+    # -- device-buffer entry points (torch tensors) --
+    def spmv(self, x, y, kernel: int = CSR_SCALAR, lanes: int = 4, block: int = 4,
+             acc: int | None = None, stream=None) -> None:
+        acc = self.dtype if acc is None else acc
+        call("spmvb_spmv", self.handle, kernel, lanes, block, C.c_void_p(x.data_ptr()),
+             C.c_void_p(y.data_ptr()), acc, _stream_ptr(stream))
+
+    def spmm(self, X, Y, k: int, tile: int = 32, bucketed: bool = False,
+             acc: int | None = None, stream=None) -> None:
+        acc = self.dtype if acc is None else acc
+        call("spmvb_spmm", self.handle, tile, int(bucketed), k, C.c_void_p(X.data_ptr()),
+             C.c_void_p(Y.data_ptr()), acc, _stream_ptr(stream))
+
+    # -- host-buffer entry points (numpy arrays; copies inside, synchronous) --
+    def spmv_host(self, x: np.ndarray, kernel: int = CSR_SCALAR, lanes: int = 4, block: int = 4,
+                  acc: int | None = None, out: np.ndarray | None = None, stream=None) -> np.ndarray:
+        acc = self.dtype if acc is None else acc
+        x = np.ascontiguousarray(x, _np_dtype(self.dtype))
+        y = out if out is not None else np.empty(self.m, _np_dtype(acc))
+        s = C.c_void_p(0) if stream is None else _stream_ptr(stream)
+        call("spmvb_spmv_host", self.handle, kernel, lanes, block, _ptr(x), _ptr(y), acc, s)
+        return y
+
+    def spmm_host(self, X: np.ndarray, k: int, tile: int = 32, bucketed: bool = False,
+                  acc: int | None = None, stream=None) -> np.ndarray:
+        acc = self.dtype if acc is None else acc
+        X = np.ascontiguousarray(X, _np_dtype(self.dtype))
+        Y = np.empty((self.m, k), _np_dtype(acc))
+        s = C.c_void_p(0) if stream is None else _stream_ptr(stream)
+        call("spmvb_spmm_host", self.handle, tile, int(bucketed), k, _ptr(X), _ptr(Y), acc, s)
+        return Y
+
+    def export_ell(self):
+        width = self.info()["max_row_nnz"]
+        col = np.zeros(self.m * width, np.int32)
+        val = np.zeros(self.m * width, _np_dtype(self.dtype))
+        rl = np.zeros(self.m, np.int32)
+        call("spmvb_matrix_export_ell", self.handle, _ptr(col), _ptr(val), _ptr(rl))
+        return width, col, val, rl
+
+    def export_bcsr(self, block: int):
+        self.prepare(BCSR, block)
+        bnnz = self.info()["bcsr2_block_nnz" if block == 2 else "bcsr4_block_nnz"]
+        mb = (self.m + block - 1) // block
+        rp = np.zeros(mb + 1, np.int32)
+        ci = np.zeros(max(bnnz, 1), np.int32)
+        va = np.zeros(max(bnnz, 1) * block * block, _np_dtype(self.dtype))
+        call("spmvb_matrix_export_bcsr", self.handle, block, _ptr(rp), _ptr(ci), _ptr(va))
+        return rp, ci[:bnnz], va[:bnnz * block * block]
+
+
+class DistMatrix:
+    """One rank's shard of a row-partitioned square matrix for iterated
+    y = A x, x <- y, with the x slices exchanged by ncclAllGather."""
+
+    def __init__(self, ctx: Context, nranks: int, rank: int, uid: bytes | None, A: CsrMatrix,
+                 bounds: np.ndarray, dtype: int = F64):
+        rp = np.ascontiguousarray(A.rowptr, np.int32)
+        ci = np.ascontiguousarray(A.colind, np.int32)
+        va = np.ascontiguousarray(A.values, _np_dtype(dtype))
+        b = np.ascontiguousarray(bounds, np.int32)
+        ub = C.create_string_buffer(uid, 128) if uid is not None else None
+        h = C.c_void_p()
+        call("spmvb_dist_create", ctx.handle, nranks, rank, ub, dtype, A.m, A.nnz, _ptr(rp),
+             _ptr(ci), _ptr(va), _ptr(b), C.byref(h))
+        self.handle = h
+        self.m = A.m
+        self.dtype = dtype
+
+    def close(self):
+        if getattr(self, "handle", None):
+            load().spmvb_dist_destroy(self.handle)
+            self.handle = None
+
+    def set_x(self, x: np.ndarray, stream=None):
+        x = np.ascontiguousarray(x, _np_dtype(self.dtype))
+        call("spmvb_dist_set_x", self.handle, _ptr(x), _stream_ptr(stream))
+
+    def iterate(self, iters: int, kernel: int = CSR_SCALAR, lanes: int = 4, stream=None):
+        call("spmvb_dist_iterate", self.handle, kernel, lanes, iters, _stream_ptr(stream))
+
+    def iterate_timed(self, iters: int, kernel: int = CSR_SCALAR, lanes: int = 4, stream=None):
+        k = C.c_double()
+        s = C.c_double()
+        call("spmvb_dist_iterate_timed", self.handle, kernel, lanes, iters, _stream_ptr(stream),
+             C.byref(k), C.byref(s))
+        return k.value, s.value
+
+    def get_x(self, stream=None) -> np.ndarray:
+        out = np.empty(self.m, _np_dtype(self.dtype))
+        call("spmvb_dist_get_x", self.handle, _ptr(out), _stream_ptr(stream))
+        return out
+
+    def info(self) -> dict:
+        a, b, c = C.c_int32(), C.c_int32(), C.c_int32()
+        d = C.c_int64()
+        call("spmvb_dist_get_info", self.handle, C.byref(a), C.byref(b), C.byref(c), C.byref(d))
+        return {"row_begin": a.value, "row_end": b.value, "max_rows": c.value, "local_nnz": d.value}

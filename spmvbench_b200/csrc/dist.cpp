@@ -1,0 +1,284 @@
+// Row-sharded multi-GPU SpMV with NCCL all-gather of x (no reference
+// counterpart; the reference is single-GPU).
+//
+// One process per GPU. Rank g owns rows [bounds[g], bounds[g+1]) of a square
+// matrix (bounds from spmvb_partition_rows, nnz-balanced). NCCL has no
+// all-gather-v, so every rank's slice of x is padded to max_rows entries and
+// x lives in a padded layout of nranks*max_rows slots: global column c owned
+// by rank r sits in slot r*max_rows + (c - bounds[r]). Columns are renumbered
+// into that layout once, when the shard is built, so each step is
+//   y_local = A_local * x_pad        (this library's SpMV kernel)
+//   x_pad   = all_gather(y_local)    (ncclAllGather over NVLink)
+// with no other copies. Communicator set-up is non-blocking with a bounded
+// wait: a rank that never joins makes spmvb_dist_create return
+// SPMVB_ERR_TIMEOUT after the communicator is aborted.
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "internal.hpp"
+
+using namespace spmvb;
+
+struct spmvb_dist_st {
+  spmvb_context ctx = nullptr;
+  int nranks = 1;
+  int rank = 0;
+  spmvb_dtype dtype = SPMVB_F64;
+  ncclComm_t comm = nullptr;
+  std::vector<int32_t> bounds;
+  int32_t m = 0;
+  int32_t max_rows = 0;
+  spmvb_matrix local = nullptr;
+  DevBuf x_pad, y_loc;
+  cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+
+  ~spmvb_dist_st() {
+    for (auto& e : ev)
+      if (e) cudaEventDestroy(e);
+    spmvb_matrix_destroy(local);
+  }
+};
+
+namespace {
+
+spmvb_status nccl_fail(ncclResult_t r, const char* what) {
+  return fail(SPMVB_ERR_NCCL, std::string(what) + ": " + ncclGetErrorString(r));
+}
+
+// Bounded wait for a non-blocking communicator operation to settle.
+spmvb_status nccl_wait(ncclComm_t comm, double timeout_s, const char* what) {
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    ncclResult_t st = ncclSuccess;
+    ncclResult_t r = ncclCommGetAsyncError(comm, &st);
+    if (r != ncclSuccess) return nccl_fail(r, what);
+    if (st == ncclSuccess) return SPMVB_OK;
+    if (st != ncclInProgress) return nccl_fail(st, what);
+    const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (el > timeout_s) return fail(SPMVB_ERR_TIMEOUT, std::string(what) + ": timed out after " + std::to_string(timeout_s) + " s");
+    std::this_thread::sleep_for(std::chrono::milliseconds(1));
+  }
+}
+
+double init_timeout_s() {
+  const char* e = std::getenv("SPMVB_NCCL_INIT_TIMEOUT_S");
+  return (e && *e) ? std::atof(e) : 120.0;
+}
+
+}  // namespace
+
+extern "C" {
+
+spmvb_status spmvb_shard_csr(int32_t m, const int32_t* h_rowptr, const int32_t* h_colind, int nranks, int rank,
+                             const int32_t* h_bounds, int32_t* max_rows, int64_t* local_nnz,
+                             int32_t* h_out_rowptr, int32_t* h_out_colind) {
+  clear_error();
+  if (!h_rowptr || !h_bounds || !max_rows || !local_nnz) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null argument");
+  if (nranks < 1 || rank < 0 || rank >= nranks || m < 0) return fail(SPMVB_ERR_INVALID_ARGUMENT, "bad rank / nranks / m");
+  if (h_bounds[0] != 0 || h_bounds[nranks] != m) return fail(SPMVB_ERR_INVALID_ARGUMENT, "bounds must span [0, m]");
+  int32_t mr = 0;
+  for (int g = 0; g < nranks; ++g) {
+    if (h_bounds[g + 1] < h_bounds[g]) return fail(SPMVB_ERR_INVALID_ARGUMENT, "bounds must be non-decreasing");
+    mr = std::max(mr, h_bounds[g + 1] - h_bounds[g]);
+  }
+  const int32_t r0 = h_bounds[rank], r1 = h_bounds[rank + 1];
+  const int64_t p0 = h_rowptr[r0], p1 = h_rowptr[r1];
+  *max_rows = mr;
+  *local_nnz = p1 - p0;
+  if (!h_out_colind) return SPMVB_OK;
+  if (!h_out_rowptr) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null output rowptr");
+  for (int32_t i = 0; i <= r1 - r0; ++i) h_out_rowptr[i] = static_cast<int32_t>(h_rowptr[r0 + i] - p0);
+  for (int64_t p = p0; p < p1; ++p) {
+    const int32_t c = h_colind[p];
+    if (c < 0 || c >= m) return fail(SPMVB_ERR_INVALID_MATRIX, "column index out of range");
+    const int owner = static_cast<int>(std::upper_bound(h_bounds, h_bounds + nranks + 1, c) - h_bounds) - 1;
+    h_out_colind[p - p0] = owner * mr + (c - h_bounds[owner]);
+  }
+  return SPMVB_OK;
+}
+
+spmvb_status spmvb_nccl_unique_id(void* h_out, size_t cap) {
+  clear_error();
+  if (!h_out || cap < sizeof(ncclUniqueId)) return fail(SPMVB_ERR_INVALID_ARGUMENT, "buffer smaller than ncclUniqueId");
+  ncclUniqueId id;
+  ncclResult_t r = ncclGetUniqueId(&id);
+  if (r != ncclSuccess) return nccl_fail(r, "ncclGetUniqueId");
+  std::memcpy(h_out, &id, sizeof(id));
+  return SPMVB_OK;
+}
+
+spmvb_status spmvb_dist_create(spmvb_context ctx, int nranks, int rank, const void* h_unique_id, spmvb_dtype dtype,
+                               int32_t m, int64_t nnz, const int32_t* h_rowptr, const int32_t* h_colind,
+                               const void* h_values, const int32_t* h_bounds, spmvb_dist* out) {
+  clear_error();
+  if (!ctx || !out || !h_rowptr || !h_bounds) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null argument");
+  if (nranks < 1 || rank < 0 || rank >= nranks) return fail(SPMVB_ERR_INVALID_ARGUMENT, "bad rank / nranks");
+  if (nranks > 1 && !h_unique_id) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null NCCL unique id");
+  if (dtype != SPMVB_F32 && dtype != SPMVB_F64) return fail(SPMVB_ERR_INVALID_ARGUMENT, "bad dtype");
+  if (m < 0 || nnz < 0 || h_rowptr[m] != nnz) return fail(SPMVB_ERR_INVALID_MATRIX, "rowptr[m] != nnz");
+  if (h_bounds[0] != 0 || h_bounds[nranks] != m) return fail(SPMVB_ERR_INVALID_ARGUMENT, "bounds must span [0, m]");
+  for (int g = 0; g < nranks; ++g)
+    if (h_bounds[g + 1] < h_bounds[g]) return fail(SPMVB_ERR_INVALID_ARGUMENT, "bounds must be non-decreasing");
+  DeviceGuard guard(ctx->device);
+  auto D = std::make_unique<spmvb_dist_st>();
+  D->ctx = ctx;
+  D->nranks = nranks;
+  D->rank = rank;
+  D->dtype = dtype;
+  D->m = m;
+  D->bounds.assign(h_bounds, h_bounds + nranks + 1);
+
+  // Local shard with renumbered columns.
+  const int32_t r0 = h_bounds[rank], r1 = h_bounds[rank + 1];
+  const int32_t ml = r1 - r0;
+  const size_t es = dtype_size(dtype);
+  int64_t lnnz = 0;
+  SPMVB_TRY(spmvb_shard_csr(m, h_rowptr, h_colind, nranks, rank, h_bounds, &D->max_rows, &lnnz, nullptr, nullptr));
+  std::vector<int32_t> rp(ml + 1), ci(std::max<int64_t>(lnnz, 1));
+  SPMVB_TRY(spmvb_shard_csr(m, h_rowptr, h_colind, nranks, rank, h_bounds, &D->max_rows, &lnnz, rp.data(), ci.data()));
+  const int64_t p0 = h_rowptr[r0];
+  const unsigned char* vv = static_cast<const unsigned char*>(h_values) + p0 * es;
+  const int32_t npad = nranks * D->max_rows;
+  SPMVB_TRY(spmvb_matrix_create_csr(ctx, dtype, ml, npad, lnnz, rp.data(), ci.data(), vv, &D->local));
+  SPMVB_TRY(D->x_pad.alloc(size_t(std::max(npad, 1)) * es));
+  SPMVB_TRY(D->y_loc.alloc(size_t(std::max(D->max_rows, 1)) * es));
+  for (auto& e : D->ev) SPMVB_TRY_CUDA(cudaEventCreate(&e));
+
+  if (nranks > 1) {
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    ncclUniqueId id;
+    std::memcpy(&id, h_unique_id, sizeof(id));
+    ncclResult_t r = ncclCommInitRankConfig(&D->comm, nranks, id, rank, &cfg);
+    if (r != ncclSuccess && r != ncclInProgress) return nccl_fail(r, "ncclCommInitRankConfig");
+    spmvb_status s = nccl_wait(D->comm, init_timeout_s(), "ncclCommInitRankConfig");
+    if (s != SPMVB_OK) {
+      const std::string msg = spmvb_last_error();
+      ncclCommAbort(D->comm);
+      D->comm = nullptr;
+      return fail(s, msg);
+    }
+  }
+  *out = D.release();
+  return SPMVB_OK;
+}
+
+spmvb_status spmvb_dist_destroy(spmvb_dist D) {
+  clear_error();
+  if (!D) return SPMVB_OK;
+  DeviceGuard g(D->ctx->device);
+  if (D->comm) {
+    ncclCommFinalize(D->comm);
+    nccl_wait(D->comm, 30.0, "ncclCommFinalize");
+    ncclCommDestroy(D->comm);
+  }
+  delete D;
+  return SPMVB_OK;
+}
+
+spmvb_status spmvb_dist_set_x(spmvb_dist D, const void* h_x, void* stream) {
+  clear_error();
+  if (!D || (D->m && !h_x)) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null argument");
+  DeviceGuard g(D->ctx->device);
+  const size_t es = dtype_size(D->dtype);
+  std::vector<unsigned char> pad(size_t(D->nranks) * D->max_rows * es, 0);
+  for (int r = 0; r < D->nranks; ++r) {
+    const int32_t b = D->bounds[r], cnt = D->bounds[r + 1] - b;
+    std::memcpy(pad.data() + size_t(r) * D->max_rows * es, static_cast<const unsigned char*>(h_x) + size_t(b) * es, size_t(cnt) * es);
+  }
+  auto s = static_cast<cudaStream_t>(stream);
+  if (!pad.empty()) SPMVB_TRY_CUDA(cudaMemcpyAsync(D->x_pad.get(), pad.data(), pad.size(), cudaMemcpyHostToDevice, s));
+  SPMVB_TRY_CUDA(cudaStreamSynchronize(s));
+  return SPMVB_OK;
+}
+
+static spmvb_status dist_step(spmvb_dist D, spmvb_kernel kernel, int lanes, cudaStream_t s) {
+  SPMVB_TRY(spmvb_spmv(D->local, kernel, lanes, 4, D->x_pad.get(), D->y_loc.get(), D->dtype, s));
+  if (D->nranks > 1) {
+    const ncclDataType_t t = D->dtype == SPMVB_F64 ? ncclFloat64 : ncclFloat32;
+    ncclResult_t r = ncclAllGather(D->y_loc.get(), D->x_pad.get(), size_t(D->max_rows), t, D->comm, s);
+    if (r != ncclSuccess && r != ncclInProgress) return nccl_fail(r, "ncclAllGather");
+  } else {
+    SPMVB_TRY_CUDA(cudaMemcpyAsync(D->x_pad.get(), D->y_loc.get(), size_t(D->max_rows) * dtype_size(D->dtype),
+                                   cudaMemcpyDeviceToDevice, s));
+  }
+  return SPMVB_OK;
+}
+
+spmvb_status spmvb_dist_iterate(spmvb_dist D, spmvb_kernel kernel, int lanes, int iters, void* stream) {
+  clear_error();
+  if (!D || iters < 0) return fail(SPMVB_ERR_INVALID_ARGUMENT, "bad argument");
+  DeviceGuard g(D->ctx->device);
+  auto s = static_cast<cudaStream_t>(stream);
+  for (int it = 0; it < iters; ++it) SPMVB_TRY(dist_step(D, kernel, lanes, s));
+  return SPMVB_OK;
+}
+
+spmvb_status spmvb_dist_iterate_timed(spmvb_dist D, spmvb_kernel kernel, int lanes, int iters, void* stream,
+                                      double* kernel_ms, double* step_ms) {
+  clear_error();
+  if (!D || iters < 0 || !kernel_ms || !step_ms) return fail(SPMVB_ERR_INVALID_ARGUMENT, "bad argument");
+  DeviceGuard g(D->ctx->device);
+  auto s = static_cast<cudaStream_t>(stream);
+  double k_ms = 0.0, st_ms = 0.0;
+  for (int it = 0; it < iters; ++it) {
+    SPMVB_TRY_CUDA(cudaEventRecord(D->ev[0], s));
+    SPMVB_TRY(spmvb_spmv(D->local, kernel, lanes, 4, D->x_pad.get(), D->y_loc.get(), D->dtype, s));
+    SPMVB_TRY_CUDA(cudaEventRecord(D->ev[1], s));
+    if (D->nranks > 1) {
+      const ncclDataType_t t = D->dtype == SPMVB_F64 ? ncclFloat64 : ncclFloat32;
+      ncclResult_t r = ncclAllGather(D->y_loc.get(), D->x_pad.get(), size_t(D->max_rows), t, D->comm, s);
+      if (r != ncclSuccess && r != ncclInProgress) return nccl_fail(r, "ncclAllGather");
+    } else {
+      SPMVB_TRY_CUDA(cudaMemcpyAsync(D->x_pad.get(), D->y_loc.get(), size_t(D->max_rows) * dtype_size(D->dtype),
+                                     cudaMemcpyDeviceToDevice, s));
+    }
+    SPMVB_TRY_CUDA(cudaEventRecord(D->ev[2], s));
+    SPMVB_TRY_CUDA(cudaEventSynchronize(D->ev[2]));
+    float a = 0.f, b = 0.f;
+    SPMVB_TRY_CUDA(cudaEventElapsedTime(&a, D->ev[0], D->ev[1]));
+    SPMVB_TRY_CUDA(cudaEventElapsedTime(&b, D->ev[0], D->ev[2]));
+    k_ms += a;
+    st_ms += b;
+  }
+  *kernel_ms = k_ms;
+  *step_ms = st_ms;
+  return SPMVB_OK;
+}
+
+spmvb_status spmvb_dist_get_x(spmvb_dist D, void* h_x, void* stream) {
+  clear_error();
+  if (!D || (D->m && !h_x)) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null argument");
+  DeviceGuard g(D->ctx->device);
+  const size_t es = dtype_size(D->dtype);
+  std::vector<unsigned char> pad(size_t(D->nranks) * D->max_rows * es);
+  auto s = static_cast<cudaStream_t>(stream);
+  if (!pad.empty()) SPMVB_TRY_CUDA(cudaMemcpyAsync(pad.data(), D->x_pad.get(), pad.size(), cudaMemcpyDeviceToHost, s));
+  SPMVB_TRY_CUDA(cudaStreamSynchronize(s));
+  for (int r = 0; r < D->nranks; ++r) {
+    const int32_t b = D->bounds[r], cnt = D->bounds[r + 1] - b;
+    std::memcpy(static_cast<unsigned char*>(h_x) + size_t(b) * es, pad.data() + size_t(r) * D->max_rows * es, size_t(cnt) * es);
+  }
+  return SPMVB_OK;
+}
+
+spmvb_status spmvb_dist_get_info(spmvb_dist D, int32_t* row_begin, int32_t* row_end, int32_t* max_rows,
+                                 int64_t* local_nnz) {
+  clear_error();
+  if (!D) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null argument");
+  if (row_begin) *row_begin = D->bounds[D->rank];
+  if (row_end) *row_end = D->bounds[D->rank + 1];
+  if (max_rows) *max_rows = D->max_rows;
+  if (local_nnz) *local_nnz = D->local->nnz;
+  return SPMVB_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,325 @@
+// Lazily built storage formats of a matrix handle.
+//
+//  ELL   - reference layout of csr_to_ell (src/formats.cpp:14-43): width =
+//          longest row, column-major slots j*m + i, padding column 0 / value
+//          0, row_lengths. Built on the device from the uploaded CSR.
+//  HYB   - new: ELL(K) holding each row's first min(len, K) entries plus a
+//          CSR tail with the rest of the rows longer than K. Built on device.
+//  BCSR  - layout of csr_to_bcsr<T,R,C> (src/formats.cpp:45-105): blocks of a
+//          block row in ascending block-column order, R*C row-major values,
+//          zero fill, and for repeated (row, column) entries the last one in
+//          CSR order wins. Built on the host with a per-block-row sort
+//          (O(L log L) instead of the reference's O(L^2) search) and uploaded.
+//  merge - merge-path tile start rows (device binary search) and the carry
+//          scratch of the merge kernel.
+//  buckets - SpMM row ids grouped by length (<= 8, <= 64, > 64), each group
+//          ascending, built on the host from rowptr.
+#include <algorithm>
+#include <cstring>
+#include <numeric>
+#include <string>
+#include <vector>
+
+#include "internal.hpp"
+#include "spmv_kernels.cuh"
+
+namespace spmvb {
+
+// ---- kernels ---------------------------------------------------------------
+__global__ void merge_partition(CsrView A, int64_t num_items, int tile_items,
+                                int num_tiles, int* __restrict__ tile_row) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t > num_tiles) return;
+  const int64_t diag = min(static_cast<int64_t>(t) * tile_items, num_items);
+  int64_t lo = diag - A.nnz > 0 ? diag - A.nnz : 0;
+  int64_t hi = diag < A.m ? diag : static_cast<int64_t>(A.m);
+  while (lo < hi) {
+    const int64_t pivot = (lo + hi) >> 1;
+    if (A.rowptr[pivot + 1] <= diag - pivot - 1)
+      lo = pivot + 1;
+    else
+      hi = pivot;
+  }
+  tile_row[t] = static_cast<int>(lo);
+}
+
+// Copies each row's first min(len, cap) entries into column-major slots and
+// records row lengths (len, or -1 when len > cap and long_marker is set).
+template <typename W>
+__global__ void ell_fill(const int* __restrict__ rowptr, const int* __restrict__ colind,
+                         const W* __restrict__ vals, int m, int cap, bool long_marker,
+                         int* __restrict__ ecol, W* __restrict__ eval,
+                         int* __restrict__ rowlen) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= m) return;
+  const int s = rowptr[r];
+  const int len = rowptr[r + 1] - s;
+  const int take = min(len, cap);
+  rowlen[r] = (long_marker && len > cap) ? -1 : len;
+  for (int j = 0; j < take; ++j) {
+    const int64_t p = static_cast<int64_t>(j) * m + r;
+    ecol[p] = colind[s + j];
+    eval[p] = vals[s + j];
+  }
+}
+
+// Copies entries K.. of each long row into the CSR tail (one warp per row).
+template <typename W>
+__global__ void hyb_tail_fill(const int* __restrict__ rowptr, const int* __restrict__ colind,
+                              const W* __restrict__ vals, const int* __restrict__ long_rows,
+                              const int* __restrict__ tail_ptr, int n_long, int K,
+                              int* __restrict__ tcol, W* __restrict__ tval) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x & 31;
+  if (w >= n_long) return;
+  const int r = long_rows[w];
+  const int s = rowptr[r] + K;
+  const int e = rowptr[r + 1];
+  const int o = tail_ptr[w];
+  for (int p = s + lane; p < e; p += 32) {
+    tcol[o + (p - s)] = colind[p];
+    tval[o + (p - s)] = vals[p];
+  }
+}
+
+namespace {
+
+template <typename W>
+void launch_ell_fill(spmvb_matrix A, int cap, bool marker, int* ecol, void* eval, int* rowlen) {
+  ell_fill<W><<<(A->m + 255) / 256, 256>>>(A->rowptr.as<int>(), A->colind.as<int>(),
+                                           A->values.as<W>(), A->m, cap, marker, ecol,
+                                           static_cast<W*>(eval), rowlen);
+  count_launch();
+}
+
+spmvb_status check_fits(spmvb_matrix A, double bytes, const char* what) {
+  size_t free_b = 0, total_b = 0;
+  SPMVB_TRY_CUDA(cudaMemGetInfo(&free_b, &total_b));
+  if (bytes > 0.85 * static_cast<double>(free_b)) {
+    char msg[256];
+    std::snprintf(msg, sizeof(msg),
+                  "%s needs %.3g GB of device memory but only %.3g GB are free "
+                  "(m=%d, longest row %d); use the hybrid ELL+CSR format",
+                  what, bytes / 1e9, free_b / 1e9, A->m, A->max_row);
+    return fail(SPMVB_ERR_UNSUPPORTED, msg);
+  }
+  return SPMVB_OK;
+}
+
+}  // namespace
+
+spmvb_status build_ell(spmvb_matrix A) {
+  std::lock_guard<std::mutex> lk(A->build_mu);
+  if (A->ell_built) return SPMVB_OK;
+  DeviceGuard g(A->device);
+  const size_t es = dtype_size(A->dtype);
+  const int64_t slots = static_cast<int64_t>(A->m) * A->max_row;
+  SPMVB_TRY(check_fits(A, static_cast<double>(slots) * (4 + es) + 4.0 * A->m, "ELL"));
+  SPMVB_TRY(A->ell_colind.alloc(std::max<int64_t>(slots, 1) * 4));
+  SPMVB_TRY(A->ell_values.alloc(std::max<int64_t>(slots, 1) * es));
+  SPMVB_TRY(A->ell_rowlen.alloc(std::max<int64_t>(A->m, 1) * 4));
+  if (A->m > 0) {
+    if (es == 8)
+      launch_ell_fill<unsigned long long>(A, A->max_row, false, A->ell_colind.as<int>(), A->ell_values.get(), A->ell_rowlen.as<int>());
+    else
+      launch_ell_fill<unsigned int>(A, A->max_row, false, A->ell_colind.as<int>(), A->ell_values.get(), A->ell_rowlen.as<int>());
+    SPMVB_TRY_CUDA(cudaGetLastError());
+    SPMVB_TRY_CUDA(cudaStreamSynchronize(0));
+  }
+  A->ell_width = A->max_row;
+  A->ell_built = true;
+  return SPMVB_OK;
+}
+
+// Automatic K: the smallest width that leaves at most m/64 rows in the tail,
+// capped so the ELL part holds at most 4x the matrix's nonzeros.
+static int choose_hyb_width(const std::vector<int32_t>& rowptr, int m, int64_t nnz, int max_row) {
+  if (m == 0) return 0;
+  std::vector<int64_t> hist(static_cast<size_t>(max_row) + 2, 0);
+  for (int i = 0; i < m; ++i) hist[rowptr[i + 1] - rowptr[i]]++;
+  const int64_t allowed = std::max<int64_t>(1, m / 64);
+  int64_t longer = m - hist[0];  // rows with len > k, for k = 0
+  int K = 0;
+  while (K < max_row && longer > allowed) {
+    ++K;
+    longer -= hist[K];
+  }
+  const int cap = static_cast<int>(std::max<int64_t>(1, (4 * nnz) / m));
+  return std::min(K, cap);
+}
+
+spmvb_status build_hyb(spmvb_matrix A, int forced_k) {
+  std::lock_guard<std::mutex> lk(A->build_mu);
+  if (A->hyb_built && (forced_k <= 0 || forced_k == A->hyb_K)) return SPMVB_OK;
+  DeviceGuard g(A->device);
+  const size_t es = dtype_size(A->dtype);
+  const int K = forced_k > 0 ? std::min(forced_k, std::max(A->max_row, 1))
+                             : choose_hyb_width(A->h_rowptr, A->m, A->nnz, A->max_row);
+  std::vector<int32_t> long_rows, tail_ptr(1, 0);
+  int64_t ell_nnz = 0;
+  for (int i = 0; i < A->m; ++i) {
+    const int len = A->h_rowptr[i + 1] - A->h_rowptr[i];
+    ell_nnz += std::min(len, K);
+    if (len > K) {
+      long_rows.push_back(i);
+      tail_ptr.push_back(tail_ptr.back() + (len - K));
+    }
+  }
+  const int64_t slots = static_cast<int64_t>(A->m) * K;
+  const int64_t tail = tail_ptr.back();
+  SPMVB_TRY(check_fits(A, static_cast<double>(slots + tail) * (4 + es) + 8.0 * A->m, "HYB"));
+  SPMVB_TRY(A->hyb_colind.alloc(std::max<int64_t>(slots, 1) * 4));
+  SPMVB_TRY(A->hyb_values.alloc(std::max<int64_t>(slots, 1) * es));
+  SPMVB_TRY(A->hyb_rowlen.alloc(std::max<int64_t>(A->m, 1) * 4));
+  SPMVB_TRY(upload(A->hyb_long_rows, long_rows.data(), long_rows.size() * 4, std::max<size_t>(long_rows.size(), 1) * 4));
+  SPMVB_TRY(upload(A->hyb_tail_ptr, tail_ptr.data(), tail_ptr.size() * 4, tail_ptr.size() * 4));
+  SPMVB_TRY(A->hyb_tail_colind.alloc((tail + kPad) * 4));
+  SPMVB_TRY(A->hyb_tail_values.alloc((tail + kPad) * es));
+  if (A->m > 0) {
+    if (es == 8)
+      launch_ell_fill<unsigned long long>(A, K, true, A->hyb_colind.as<int>(), A->hyb_values.get(), A->hyb_rowlen.as<int>());
+    else
+      launch_ell_fill<unsigned int>(A, K, true, A->hyb_colind.as<int>(), A->hyb_values.get(), A->hyb_rowlen.as<int>());
+    const int n_long = static_cast<int>(long_rows.size());
+    if (n_long > 0) {
+      const int grid = (n_long + 7) / 8;
+      if (es == 8)
+        hyb_tail_fill<unsigned long long><<<grid, 256>>>(A->rowptr.as<int>(), A->colind.as<int>(), A->values.as<unsigned long long>(),
+                                                         A->hyb_long_rows.as<int>(), A->hyb_tail_ptr.as<int>(), n_long, K,
+                                                         A->hyb_tail_colind.as<int>(), A->hyb_tail_values.as<unsigned long long>());
+      else
+        hyb_tail_fill<unsigned int><<<grid, 256>>>(A->rowptr.as<int>(), A->colind.as<int>(), A->values.as<unsigned int>(),
+                                                   A->hyb_long_rows.as<int>(), A->hyb_tail_ptr.as<int>(), n_long, K,
+                                                   A->hyb_tail_colind.as<int>(), A->hyb_tail_values.as<unsigned int>());
+      count_launch();
+    }
+    SPMVB_TRY_CUDA(cudaGetLastError());
+    SPMVB_TRY_CUDA(cudaStreamSynchronize(0));
+  }
+  A->hyb_K = K;
+  A->hyb_ell_nnz = ell_nnz;
+  A->hyb_tail_nnz = tail;
+  A->hyb_n_long = static_cast<int>(long_rows.size());
+  A->hyb_built = true;
+  return SPMVB_OK;
+}
+
+// Host CSR -> BCSR with the reference's layout rules.
+template <typename V>
+static void csr_to_bcsr_host(const spmvb_matrix A, int R, int C, std::vector<int32_t>& browptr,
+                             std::vector<int32_t>& bcol, std::vector<V>& bval) {
+  const int m = A->m;
+  const int mb = (m + R - 1) / R;
+  const V* vals = reinterpret_cast<const V*>(A->h_values.data());
+  browptr.assign(static_cast<size_t>(mb) + 1, 0);
+  bcol.clear();
+  bval.clear();
+  struct Ent {
+    int32_t bj;
+    int32_t slot;  // r*C + cc
+    int64_t p;
+  };
+  std::vector<Ent> ents;
+  for (int bi = 0; bi < mb; ++bi) {
+    ents.clear();
+    for (int r = 0; r < R; ++r) {
+      const int i = bi * R + r;
+      if (i >= m) break;
+      for (int32_t p = A->h_rowptr[i]; p < A->h_rowptr[i + 1]; ++p) {
+        const int32_t col = A->h_colind[p];
+        ents.push_back({col / C, r * C + col % C, p});
+      }
+    }
+    // Ascending block column; within a block the CSR order (r, then p) is
+    // kept, so the last write of a repeated (row, column) wins.
+    std::stable_sort(ents.begin(), ents.end(), [](const Ent& a, const Ent& b) { return a.bj < b.bj; });
+    size_t a = 0;
+    while (a < ents.size()) {
+      size_t b = a;
+      const size_t base = bval.size();
+      bval.resize(base + static_cast<size_t>(R) * C, V(0));
+      bcol.push_back(ents[a].bj);
+      while (b < ents.size() && ents[b].bj == ents[a].bj) {
+        bval[base + ents[b].slot] = vals[ents[b].p];
+        ++b;
+      }
+      a = b;
+    }
+    browptr[bi + 1] = static_cast<int32_t>(bcol.size());
+  }
+}
+
+spmvb_status build_bcsr(spmvb_matrix A, int block) {
+  std::lock_guard<std::mutex> lk(A->build_mu);
+  auto& B = block == 2 ? A->bcsr2 : A->bcsr4;
+  if (B.built) return SPMVB_OK;
+  DeviceGuard g(A->device);
+  std::vector<int32_t> browptr, bcol;
+  const size_t es = dtype_size(A->dtype);
+  std::vector<unsigned char> bytes;
+  if (es == 8) {
+    std::vector<double> v;
+    csr_to_bcsr_host<double>(A, block, block, browptr, bcol, v);
+    bytes.assign(reinterpret_cast<unsigned char*>(v.data()), reinterpret_cast<unsigned char*>(v.data() + v.size()));
+  } else {
+    std::vector<float> v;
+    csr_to_bcsr_host<float>(A, block, block, browptr, bcol, v);
+    bytes.assign(reinterpret_cast<unsigned char*>(v.data()), reinterpret_cast<unsigned char*>(v.data() + v.size()));
+  }
+  SPMVB_TRY(check_fits(A, static_cast<double>(bytes.size() + bcol.size() * 4 + browptr.size() * 4), "BCSR"));
+  SPMVB_TRY(upload(B.rowptr, browptr.data(), browptr.size() * 4, browptr.size() * 4));
+  SPMVB_TRY(upload(B.colind, bcol.data(), bcol.size() * 4, (bcol.size() + kPad) * 4));
+  SPMVB_TRY(upload(B.values, bytes.data(), bytes.size(), bytes.size() + kPad * es));
+  B.mb = static_cast<int>(browptr.size()) - 1;
+  B.block_nnz = static_cast<int64_t>(bcol.size());
+  B.built = true;
+  return SPMVB_OK;
+}
+
+spmvb_status build_merge(spmvb_matrix A) {
+  std::lock_guard<std::mutex> lk(A->build_mu);
+  if (A->merge_built) return SPMVB_OK;
+  DeviceGuard g(A->device);
+  const int64_t items = static_cast<int64_t>(A->m) + A->nnz;
+  const int64_t tiles = (items + kMergeTile - 1) / kMergeTile;
+  if (tiles > INT32_MAX - 1) return fail(SPMVB_ERR_UNSUPPORTED, "too many merge tiles");
+  A->merge_tiles = static_cast<int>(tiles);
+  SPMVB_TRY(A->merge_tile_row.alloc((tiles + 1) * 4));
+  SPMVB_TRY(A->merge_carry_row.alloc(std::max<int64_t>(tiles, 1) * 4));
+  SPMVB_TRY(A->merge_carry_val.alloc(std::max<int64_t>(tiles, 1) * 8));
+  if (tiles > 0) {
+    merge_partition<<<static_cast<int>((tiles + 1 + 255) / 256), 256>>>(
+        A->csr_view(), items, kMergeTile, static_cast<int>(tiles), A->merge_tile_row.as<int>());
+    count_launch();
+    SPMVB_TRY_CUDA(cudaGetLastError());
+    SPMVB_TRY_CUDA(cudaStreamSynchronize(0));
+  }
+  A->merge_built = true;
+  return SPMVB_OK;
+}
+
+spmvb_status build_buckets(spmvb_matrix A) {
+  std::lock_guard<std::mutex> lk(A->build_mu);
+  if (A->buckets_built) return SPMVB_OK;
+  DeviceGuard g(A->device);
+  std::vector<int32_t> s, md, l;
+  for (int i = 0; i < A->m; ++i) {
+    const int len = A->h_rowptr[i + 1] - A->h_rowptr[i];
+    if (len <= 8) s.push_back(i);
+    else if (len <= 64) md.push_back(i);
+    else l.push_back(i);
+  }
+  std::vector<int32_t> rows;
+  rows.reserve(A->m);
+  rows.insert(rows.end(), s.begin(), s.end());
+  rows.insert(rows.end(), md.begin(), md.end());
+  rows.insert(rows.end(), l.begin(), l.end());
+  SPMVB_TRY(upload(A->bucket_rows, rows.data(), rows.size() * 4, std::max<size_t>(rows.size(), 1) * 4));
+  A->b_short = static_cast<int>(s.size());
+  A->b_med = static_cast<int>(md.size());
+  A->b_long = static_cast<int>(l.size());
+  A->buckets_built = true;
+  return SPMVB_OK;
+}
+
+}  // namespace spmvb

@@ -1,0 +1,186 @@
+// Host-side internals of libspmvb: status plumbing, device buffers, and the
+// context / matrix handles behind the C ABI (include/spmvb.h).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/spmvb.h"
+#include "views.hpp"
+
+namespace spmvb {
+
+// ---- status / errors -------------------------------------------------------
+// Records `msg` as this thread's last error and returns `s`.
+spmvb_status fail(spmvb_status s, const std::string& msg);
+spmvb_status cuda_fail(cudaError_t e, const char* what);
+void clear_error();
+
+extern std::atomic<uint64_t> g_launches;
+inline void count_launch(uint64_t n = 1) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+#define SPMVB_TRY_CUDA(expr)                                  \
+  do {                                                        \
+    cudaError_t _e = (expr);                                  \
+    if (_e != cudaSuccess) return ::spmvb::cuda_fail(_e, #expr); \
+  } while (0)
+
+#define SPMVB_TRY(expr)                          \
+  do {                                           \
+    spmvb_status _s = (expr);                    \
+    if (_s != SPMVB_OK) return _s;               \
+  } while (0)
+
+// Switches to `dev` for the lifetime of the guard.
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev_);
+    if (prev_ != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != prev_) cudaSetDevice(prev_);
+  }
+  DeviceGuard(const DeviceGuard&) = delete;
+  DeviceGuard& operator=(const DeviceGuard&) = delete;
+
+ private:
+  int prev_ = 0;
+};
+
+// Owning device allocation.
+class DevBuf {
+ public:
+  DevBuf() = default;
+  ~DevBuf() { reset(); }
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  DevBuf(DevBuf&& o) noexcept : p_(o.p_), bytes_(o.bytes_) { o.p_ = nullptr; o.bytes_ = 0; }
+  DevBuf& operator=(DevBuf&& o) noexcept {
+    if (this != &o) { reset(); p_ = o.p_; bytes_ = o.bytes_; o.p_ = nullptr; o.bytes_ = 0; }
+    return *this;
+  }
+  spmvb_status alloc(size_t bytes);  // zero-filled
+  void reset();
+  void* get() const { return p_; }
+  template <typename U> U* as() const { return static_cast<U*>(p_); }
+  size_t bytes() const { return bytes_; }
+
+ private:
+  void* p_ = nullptr;
+  size_t bytes_ = 0;
+};
+
+// Upload host bytes into a fresh zero-filled buffer of at least `cap` bytes.
+spmvb_status upload(DevBuf& dst, const void* src, size_t bytes, size_t cap);
+
+inline size_t dtype_size(spmvb_dtype d) { return d == SPMVB_F64 ? 8 : 4; }
+
+}  // namespace spmvb
+
+struct spmvb_context_st {
+  int device = 0;
+  int sm_count = 0;
+  int l2_bytes = 0;
+  int max_smem_optin = 0;
+};
+
+struct spmvb_matrix_st {
+  spmvb_context ctx = nullptr;
+  int device = 0;
+  spmvb_dtype dtype = SPMVB_F64;
+  int m = 0;
+  int n = 0;
+  int64_t nnz = 0;
+  int max_row = 0;
+
+  // Host copy of the CSR arrays (the reference's SpmvRunner also keeps one,
+  // src/cuda/spmv_cuda.cu:147). Lazily built formats are derived from it.
+  std::vector<int32_t> h_rowptr;
+  std::vector<int32_t> h_colind;
+  std::vector<unsigned char> h_values;
+
+  spmvb::DevBuf rowptr, colind, values;
+
+  // ELL (reference layout, ld = m)
+  bool ell_built = false;
+  int ell_width = 0;
+  spmvb::DevBuf ell_colind, ell_values, ell_rowlen;
+
+  // Hybrid ELL(K) + CSR tail
+  bool hyb_built = false;
+  int hyb_K = 0;
+  int64_t hyb_ell_nnz = 0, hyb_tail_nnz = 0;
+  int hyb_n_long = 0;
+  spmvb::DevBuf hyb_colind, hyb_values, hyb_rowlen, hyb_long_rows, hyb_tail_ptr,
+      hyb_tail_colind, hyb_tail_values;
+
+  // BCSR 2x2 and 4x4
+  struct Bcsr {
+    bool built = false;
+    int mb = 0;
+    int64_t block_nnz = 0;
+    spmvb::DevBuf rowptr, colind, values;
+  } bcsr2, bcsr4;
+
+  // Merge-path partition + carry scratch (sized for the widest accumulator)
+  bool merge_built = false;
+  int merge_tiles = 0;
+  spmvb::DevBuf merge_tile_row, merge_carry_row, merge_carry_val;
+
+  // SpMM row buckets
+  bool buckets_built = false;
+  int b_short = 0, b_med = 0, b_long = 0;
+  spmvb::DevBuf bucket_rows;
+
+  // Staging buffers for the host-buffer entry points
+  spmvb::DevBuf stage_in, stage_out;
+
+  std::mutex build_mu;
+
+  spmvb::CsrView csr_view() const {
+    spmvb::CsrView v;
+    v.rowptr = rowptr.as<int>();
+    v.colind = colind.as<int>();
+    v.values = values.get();
+    v.m = m;
+    v.n = n;
+    v.nnz = nnz;
+    return v;
+  }
+  int64_t device_bytes() const;
+};
+
+namespace spmvb {
+
+// Lazy builders (formats.cpp). Each is idempotent and thread safe.
+spmvb_status build_ell(spmvb_matrix A);
+spmvb_status build_hyb(spmvb_matrix A, int forced_k);
+spmvb_status build_bcsr(spmvb_matrix A, int block);
+spmvb_status build_merge(spmvb_matrix A);
+spmvb_status build_buckets(spmvb_matrix A);
+
+// Merge-path tile shape shared by the partition builder and the kernel.
+constexpr int kMergeThreads = 256;
+constexpr int kMergeIpt = 7;
+constexpr int kMergeTile = kMergeThreads * kMergeIpt;
+
+// Device launchers, one instantiation per (T, Acc) in spmv_<t><acc>.cu.
+template <typename T, typename Acc>
+spmvb_status launch_spmv(spmvb_matrix A, spmvb_kernel kernel, int lanes,
+                         int block, const T* x, Acc* y, cudaStream_t stream);
+template <typename T, typename Acc>
+spmvb_status launch_spmm(spmvb_matrix A, int tile, int bucketed, int k,
+                         const T* X, Acc* Y, cudaStream_t stream);
+spmvb_status launch_merge_partition(spmvb_matrix A, cudaStream_t stream);
+
+}  // namespace spmvb

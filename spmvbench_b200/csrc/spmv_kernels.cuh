@@ -1,0 +1,511 @@
+// SpMV kernels for sm_100a. Templated on the storage type T and the
+// accumulator type Acc, like the reference kernels (src/cuda/spmv_cuda.cu).
+//
+// Kernel map (reference kernel -> this file):
+//   csr_scalar_kernel (spmv_cuda.cu:43-54)   -> csr_scalar_staged
+//   csr_vector_kernel (spmv_cuda.cu:56-80)   -> csr_vector<G>
+//   csr_warp_kernel   (spmv_cuda.cu:83-97)   -> csr_vector<32>
+//   csr_merge_kernel  (spmv_cuda.cu:100-125) -> csr_merge + merge_fixup (a real
+//                                              merge-path, not a row queue)
+//   ell_kernel        (spmv_cuda.cu:128-142) -> ell_rows
+//   bcsr_kernel       (spmv_cuda.cu:145-170) -> bcsr_rows
+//   (new) hybrid ELL(K)+CSR tail            -> ell_rows<skip long> + hyb_long_rows
+//
+// Summation order. csr_scalar_staged, ell_rows and hyb's ELL part add each
+// row's terms left to right from zero with separately rounded multiply and
+// add, exactly as csr_omp does (src/cpu/spmv_cpu.cpp:19-25), so their output
+// is bit-identical to it. bcsr_rows follows spmv_bcsr_cpu's order
+// (src/cpu/spmv_cpu.cpp:85-97: per-block partial, then added), so it is
+// bit-identical to that kernel. The vector/warp/merge/long-row kernels
+// re-associate the sum and are bounded by 2*gamma_n*sum|a_ij x_j|
+// (tests/test_cuda_correctness.cpp:1-11 of the reference).
+#pragma once
+
+#include <climits>
+#include <cstdint>
+
+#include "common.cuh"
+#include "views.hpp"
+
+namespace spmvb {
+
+// Shared-memory slot of staged product q. One pad word per 16 doubles (per 32
+// floats) keeps thread-per-row reads of 16-entry rows conflict free.
+template <typename Acc>
+__device__ __forceinline__ int swz(int q) {
+  return sizeof(Acc) == 8 ? q + (q >> 4) : q + (q >> 5);
+}
+template <typename Acc>
+constexpr int swz_size(int cap) {
+  return sizeof(Acc) == 8 ? cap + cap / 16 + 1 : cap + cap / 32 + 1;
+}
+
+// Load 4 consecutive values starting at a 4-aligned index.
+__device__ __forceinline__ void ld_stream_quad(const double* p, uint64_t pol,
+                                               double (&v)[4]) {
+  const double2 a = ld_stream2(p, pol);
+  const double2 b = ld_stream2(p + 2, pol);
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+__device__ __forceinline__ void ld_stream_quad(const float* p, uint64_t pol,
+                                               float (&v)[4]) {
+  const float4 a = ld_stream4(p, pol);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+}
+
+// Products Acc(values[p]) * Acc(x[colind[p]]) for p in [c0, c1), c0 a
+// multiple of 4, written to s_prod[swz(p - c0)]. Threads take groups of 4
+// consecutive entries, so a warp reads 512 contiguous bytes of colind with
+// one 16-byte load per lane. Entries up to the next multiple of 4 past c1
+// are computed too (the arrays carry kPad padding); callers ignore them.
+// GROUPS = groups of 4 per thread per pass, all loads of a pass are issued
+// before any product is formed.
+template <typename T, typename Acc, int NT, int GROUPS>
+__device__ __forceinline__ void stage_products(
+    const int* __restrict__ colind, const T* __restrict__ vals,
+    const T* __restrict__ x, int64_t c0, int64_t c1, Acc* s_prod,
+    uint64_t pol_stream, uint64_t pol_keep) {
+  const int span = static_cast<int>(c1 - c0);
+  for (int base = 0; base < span; base += NT * 4 * GROUPS) {
+    int4 c[GROUPS];
+    bool ok[GROUPS];
+#pragma unroll
+    for (int g = 0; g < GROUPS; ++g) {
+      const int q = base + (g * NT + static_cast<int>(threadIdx.x)) * 4;
+      ok[g] = q < span;
+      c[g] = ok[g] ? ld_stream4(colind + c0 + q, pol_stream)
+                   : make_int4(0, 0, 0, 0);
+    }
+    T xv[GROUPS][4];
+#pragma unroll
+    for (int g = 0; g < GROUPS; ++g) {
+      if (ok[g]) {
+        xv[g][0] = ld_keep(x + c[g].x, pol_keep);
+        xv[g][1] = ld_keep(x + c[g].y, pol_keep);
+        xv[g][2] = ld_keep(x + c[g].z, pol_keep);
+        xv[g][3] = ld_keep(x + c[g].w, pol_keep);
+      }
+    }
+    T av[GROUPS][4];
+#pragma unroll
+    for (int g = 0; g < GROUPS; ++g) {
+      const int q = base + (g * NT + static_cast<int>(threadIdx.x)) * 4;
+      if (ok[g]) ld_stream_quad(vals + c0 + q, pol_stream, av[g]);
+    }
+#pragma unroll
+    for (int g = 0; g < GROUPS; ++g) {
+      const int q = base + (g * NT + static_cast<int>(threadIdx.x)) * 4;
+      if (ok[g]) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          s_prod[swz<Acc>(q + i)] = prod<Acc>(av[g][i], xv[g][i]);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CSR scalar: one row per thread, csr_omp summation order, coalesced loads.
+// A CTA owns NT consecutive rows. Their nonzeros (a contiguous range of the
+// CSR arrays) are streamed through shared memory in chunks of CAP products;
+// each thread then adds its own row's products in order. A row longer than a
+// chunk simply continues its running sum across chunks.
+// ---------------------------------------------------------------------------
+template <typename T, typename Acc, int NT, int CAP>
+__global__ void __launch_bounds__(NT)
+    csr_scalar_staged(CsrView A, const T* __restrict__ x, Acc* __restrict__ y) {
+  static_assert(CAP % (NT * 4) == 0, "CAP must be a multiple of 4*NT");
+  __shared__ int s_rp[NT + 1];
+  __shared__ Acc s_prod[swz_size<Acc>(CAP)];
+  const T* __restrict__ vals = static_cast<const T*>(A.values);
+  const uint64_t ps = policy_evict_first();
+  const uint64_t pk = policy_evict_last();
+  const int t = threadIdx.x;
+  const int num_tiles = (A.m + NT - 1) / NT;
+  for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    const int r0 = tile * NT;
+    const int nr = min(NT, A.m - r0);
+    for (int i = t; i <= nr; i += NT) s_rp[i] = A.rowptr[r0 + i];
+    __syncthreads();
+    const int64_t pbeg = s_rp[0];
+    const int64_t pend = s_rp[nr];
+    int64_t my_s = 0, my_e = 0;
+    if (t < nr) {
+      my_s = s_rp[t];
+      my_e = s_rp[t + 1];
+    }
+    Acc sum = Acc(0);
+    for (int64_t c0 = pbeg & ~int64_t(3); c0 < pend; c0 += CAP) {
+      const int64_t c1 = min(c0 + CAP, pend);
+      stage_products<T, Acc, NT, CAP / (NT * 4)>(A.colind, vals, x, c0, c1,
+                                                 s_prod, ps, pk);
+      __syncthreads();
+      const int a = static_cast<int>(max(my_s, c0) - c0);
+      const int b = static_cast<int>(min(my_e, c1) - c0);
+      for (int q = a; q < b; ++q) sum = add_rn(sum, s_prod[swz<Acc>(q)]);
+      __syncthreads();
+    }
+    if (t < nr) y[r0 + t] = sum;
+    __syncthreads();  // s_rp is rewritten by the next tile
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CSR vector: G lanes per row (G = 2..32; G = 32 is the warp kernel). Lanes
+// of a group read the row with 16-byte vector loads (2 doubles / 4 floats
+// and the matching column indices) after a scalar head that reaches vector
+// alignment, then reduce with a butterfly. Trip counts are warp-uniform so
+// the full-mask shuffles are always legal.
+// ---------------------------------------------------------------------------
+template <typename T, typename Acc, int G>
+__global__ void __launch_bounds__(256)
+    csr_vector(CsrView A, const T* __restrict__ x, Acc* __restrict__ y) {
+  constexpr int V = 16 / sizeof(T);  // elements per vector load
+  constexpr int RPW = kWarp / G;     // rows per warp per iteration
+  const T* __restrict__ vals = static_cast<const T*>(A.values);
+  const uint64_t ps = policy_evict_first();
+  const uint64_t pk = policy_evict_last();
+  const int lane = threadIdx.x & (kWarp - 1);
+  const int gl = lane & (G - 1);
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / kWarp;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * blockDim.x / kWarp;
+  for (int64_t r0 = warp * RPW; r0 < A.m; r0 += nwarps * RPW) {
+    const int64_t row = r0 + lane / G;
+    Acc sum = Acc(0);
+    if (row < A.m) {
+      const int s = A.rowptr[row];
+      const int e = A.rowptr[row + 1];
+      const int head_end = min(e, (s + V - 1) & ~(V - 1));
+      if (s + gl < head_end)
+        sum = add_rn(sum, prod<Acc>(ld_stream(vals + s + gl, ps),
+                                    ld_keep(x + ld_stream(A.colind + s + gl, ps), pk)));
+      const int nvec = (e - head_end) / V;  // full vectors after the head
+      const int body_end = head_end + nvec * V;
+#pragma unroll 2
+      for (int q = head_end + gl * V; q < body_end; q += G * V) {
+        if constexpr (V == 2) {
+          const int2 c = ld_stream2(A.colind + q, ps);
+          const double2 a = ld_stream2(reinterpret_cast<const double*>(vals) + q, ps);
+          const T x0 = ld_keep(x + c.x, pk);
+          const T x1 = ld_keep(x + c.y, pk);
+          sum = add_rn(sum, prod<Acc>(static_cast<T>(a.x), x0));
+          sum = add_rn(sum, prod<Acc>(static_cast<T>(a.y), x1));
+        } else {
+          const int4 c = ld_stream4(A.colind + q, ps);
+          const float4 a = ld_stream4(reinterpret_cast<const float*>(vals) + q, ps);
+          const T x0 = ld_keep(x + c.x, pk);
+          const T x1 = ld_keep(x + c.y, pk);
+          const T x2 = ld_keep(x + c.z, pk);
+          const T x3 = ld_keep(x + c.w, pk);
+          sum = add_rn(sum, prod<Acc>(static_cast<T>(a.x), x0));
+          sum = add_rn(sum, prod<Acc>(static_cast<T>(a.y), x1));
+          sum = add_rn(sum, prod<Acc>(static_cast<T>(a.z), x2));
+          sum = add_rn(sum, prod<Acc>(static_cast<T>(a.w), x3));
+        }
+      }
+      if (body_end + gl < e)
+        sum = add_rn(sum, prod<Acc>(ld_stream(vals + body_end + gl, ps),
+                                    ld_keep(x + ld_stream(A.colind + body_end + gl, ps), pk)));
+    }
+    sum = group_sum<G>(sum);
+    if (row < A.m && gl == 0) y[row] = sum;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CSR merge-path (Merrill & Garland, "Merge-based parallel sparse
+// matrix-vector multiplication", SC'16): the merge of the m row-end offsets
+// with the nnz entry indices is cut into tiles of NT*IPT consecutive items,
+// so every thread gets IPT items whatever the row lengths. A CTA stages its
+// tile's row ends and products in shared memory with coalesced loads, then
+// each thread walks its IPT items. Partial row sums that cross threads are
+// combined in thread order; a partial that crosses into the next tile is
+// written to the carry scratch and added by merge_fixup in tile order, so
+// results are deterministic run to run.
+// ---------------------------------------------------------------------------
+template <int NT, int IPT>
+struct MergeShape {
+  static constexpr int kTile = NT * IPT;
+};
+
+template <typename T, typename Acc, int NT, int IPT>
+__global__ void __launch_bounds__(NT)
+    csr_merge(CsrView A, MergeView M, const T* __restrict__ x, Acc* __restrict__ y) {
+  constexpr int TILE = NT * IPT;
+  __shared__ int s_rowend[TILE + 1];
+  __shared__ Acc s_prod[swz_size<Acc>(TILE + 8)];
+  __shared__ int s_crow[NT];
+  __shared__ Acc s_cval[NT];
+  const T* __restrict__ vals = static_cast<const T*>(A.values);
+  const uint64_t ps = policy_evict_first();
+  const uint64_t pk = policy_evict_last();
+  const int t = threadIdx.x;
+  const int tile = blockIdx.x;
+  const int64_t d0 = static_cast<int64_t>(tile) * TILE;
+  const int64_t d1 = min(d0 + TILE, M.num_items);
+  const int row0 = M.tile_row[tile];
+  const int row1 = M.tile_row[tile + 1];
+  const int64_t j0 = d0 - row0;
+  const int64_t j1 = d1 - row1;
+  const int nrows_local = row1 - row0;          // row ends inside the tile
+  const int nnz_local = static_cast<int>(j1 - j0);
+
+  for (int i = t; i <= nrows_local; i += NT) {
+    const int r = row0 + i;
+    s_rowend[i] = (r < A.m) ? A.rowptr[r + 1] : INT_MAX;
+  }
+  const int64_t pa = j0 & ~int64_t(3);
+  stage_products<T, Acc, NT, 2>(A.colind, vals, x, pa, j1, s_prod, ps, pk);
+  __syncthreads();
+
+  // Merge-path search for this thread's start inside the tile.
+  const int items = static_cast<int>(d1 - d0);
+  const int k = min(t * IPT, items);
+  int lo = max(0, k - nnz_local);
+  int hi = min(k, nrows_local);
+  while (lo < hi) {
+    const int pivot = (lo + hi) >> 1;
+    if (s_rowend[pivot] <= j0 + k - pivot - 1)
+      lo = pivot + 1;
+    else
+      hi = pivot;
+  }
+  int row = row0 + lo;
+  int64_t nz = j0 + k - lo;
+  const int start_row = row;
+  const int my_items = min(IPT, items - k);
+
+  Acc sum = Acc(0);
+  bool have = false;       // consumed an entry of `row` since it started
+  int held_row = -1;       // first completed row, if it is the start row
+  Acc held_val = Acc(0);
+  for (int i = 0; i < my_items; ++i) {
+    if (nz < s_rowend[row - row0]) {
+      sum = add_rn(sum, s_prod[swz<Acc>(static_cast<int>(nz - pa))]);
+      have = true;
+      ++nz;
+    } else {
+      if (row == start_row && held_row < 0) {
+        held_row = row;
+        held_val = sum;
+      } else {
+        y[row] = sum;
+      }
+      sum = Acc(0);
+      have = false;
+      ++row;
+    }
+  }
+  s_crow[t] = have ? row : -1;
+  s_cval[t] = sum;
+  __syncthreads();
+
+  if (held_row >= 0) {
+    int t0 = t;
+    while (t0 > 0 && s_crow[t0 - 1] == held_row) --t0;
+    if (t0 < t) {
+      Acc c = s_cval[t0];
+      for (int u = t0 + 1; u < t; ++u) c = add_rn(c, s_cval[u]);
+      y[held_row] = add_rn(c, held_val);
+    } else {
+      y[held_row] = held_val;
+    }
+  }
+  if (t == NT - 1) {
+    const int r = s_crow[NT - 1];
+    if (r >= 0) {
+      int t0 = NT - 1;
+      while (t0 > 0 && s_crow[t0 - 1] == r) --t0;
+      Acc c = s_cval[t0];
+      for (int u = t0 + 1; u < NT; ++u) c = add_rn(c, s_cval[u]);
+      M.carry_row[tile] = r;
+      static_cast<Acc*>(M.carry_val)[tile] = c;
+    } else {
+      M.carry_row[tile] = -1;
+    }
+  }
+}
+
+// Adds the carries of consecutive tiles that end inside the same row, in tile
+// order, to the row's value written by the tile that completed it.
+template <typename Acc>
+__global__ void merge_fixup(MergeView M, Acc* __restrict__ y) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= M.num_tiles) return;
+  const int r = M.carry_row[b];
+  if (r < 0) return;
+  if (b > 0 && M.carry_row[b - 1] == r) return;  // not the first of the run
+  const Acc* cv = static_cast<const Acc*>(M.carry_val);
+  Acc s = cv[b];
+  for (int u = b + 1; u < M.num_tiles && M.carry_row[u] == r; ++u)
+    s = add_rn(s, cv[u]);
+  y[r] = add_rn(y[r], s);
+}
+
+// Tile start rows of the merge path: for diagonal d = t*tile_items, the
+// number of row ends that precede it (binary search over rowptr).
+__global__ void merge_partition(CsrView A, int64_t num_items, int tile_items,
+                                int num_tiles, int* __restrict__ tile_row);
+
+// ---------------------------------------------------------------------------
+// ELL: one row per thread, column-major slots j*ld + row (coalesced across
+// the warp), only the row's real entries are read (row_lengths), csr_omp
+// order. SKIP_LONG: rows with row_lengths < 0 belong to the hybrid format's
+// long-row kernel and are not written here.
+// ---------------------------------------------------------------------------
+template <typename T, typename Acc, bool SKIP_LONG>
+__global__ void __launch_bounds__(256)
+    ell_rows(EllView E, const T* __restrict__ x, Acc* __restrict__ y) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= E.m) return;
+  const T* __restrict__ vals = static_cast<const T*>(E.values);
+  const uint64_t ps = policy_evict_first();
+  const uint64_t pk = policy_evict_last();
+  const int L = E.row_lengths[row];
+  if (SKIP_LONG && L < 0) return;
+  Acc sum = Acc(0);
+  int64_t p = row;
+  int j = 0;
+  for (; j + 4 <= L; j += 4) {
+    int c[4];
+    T a[4], xv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) c[u] = ld_stream(E.colind + p + u * E.ld, ps);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) a[u] = ld_stream(vals + p + u * E.ld, ps);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) xv[u] = ld_keep(x + c[u], pk);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) sum = add_rn(sum, prod<Acc>(a[u], xv[u]));
+    p += 4 * E.ld;
+  }
+  for (; j < L; ++j) {
+    sum = add_rn(sum, prod<Acc>(ld_stream(vals + p, ps),
+                                ld_keep(x + ld_stream(E.colind + p, ps), pk)));
+    p += E.ld;
+  }
+  y[row] = sum;
+}
+
+// Hybrid long rows: one warp per row over its K ELL slots and its CSR tail.
+template <typename T, typename Acc>
+__global__ void __launch_bounds__(256)
+    hyb_long_rows(HybView H, const T* __restrict__ x, Acc* __restrict__ y) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) / kWarp;
+  const int lane = threadIdx.x & (kWarp - 1);
+  if (w >= H.n_long) return;
+  const uint64_t ps = policy_evict_first();
+  const uint64_t pk = policy_evict_last();
+  const int row = H.long_rows[w];
+  const T* __restrict__ ev = static_cast<const T*>(H.ell.values);
+  const T* __restrict__ tv = static_cast<const T*>(H.tail_values);
+  Acc sum = Acc(0);
+  for (int j = lane; j < H.ell.width; j += kWarp) {
+    const int64_t p = static_cast<int64_t>(j) * H.ell.ld + row;
+    sum = add_rn(sum, prod<Acc>(ld_stream(ev + p, ps),
+                                ld_keep(x + ld_stream(H.ell.colind + p, ps), pk)));
+  }
+  const int s = H.tail_ptr[w];
+  const int e = H.tail_ptr[w + 1];
+#pragma unroll 4
+  for (int p = s + lane; p < e; p += kWarp)
+    sum = add_rn(sum, prod<Acc>(ld_stream(tv + p, ps),
+                                ld_keep(x + ld_stream(H.tail_colind + p, ps), pk)));
+  sum = group_sum<kWarp>(sum);
+  if (lane == 0) y[row] = sum;
+}
+
+// ---------------------------------------------------------------------------
+// BCSR R x C: one thread per (block row, r). The R threads of a block row
+// read its blocks' rows (C contiguous values, one or two 16-byte loads) and
+// share the C-wide slice of x. Order per row: per-block partial over c, then
+// added to the row total (spmv_bcsr_cpu order). VEC_X: x is 16-byte aligned
+// so full slices are vector loads; the last partial block column is read
+// element by element with the column bound the reference applies.
+// ---------------------------------------------------------------------------
+template <typename T, int C>
+struct BlockRow;
+template <>
+struct BlockRow<double, 4> {
+  __device__ static void load(const double* p, uint64_t pol, double (&v)[4]) {
+    const double2 a = ld_stream2(p, pol), b = ld_stream2(p + 2, pol);
+    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+  }
+  __device__ static void load_x(const double* p, uint64_t pol, double (&v)[4]) {
+    const double2 a = ld_keep2(p, pol), b = ld_keep2(p + 2, pol);
+    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+  }
+};
+template <>
+struct BlockRow<double, 2> {
+  __device__ static void load(const double* p, uint64_t pol, double (&v)[2]) {
+    const double2 a = ld_stream2(p, pol);
+    v[0] = a.x; v[1] = a.y;
+  }
+  __device__ static void load_x(const double* p, uint64_t pol, double (&v)[2]) {
+    const double2 a = ld_keep2(p, pol);
+    v[0] = a.x; v[1] = a.y;
+  }
+};
+template <>
+struct BlockRow<float, 4> {
+  __device__ static void load(const float* p, uint64_t pol, float (&v)[4]) {
+    const float4 a = ld_stream4(p, pol);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  }
+  __device__ static void load_x(const float* p, uint64_t pol, float (&v)[4]) {
+    const float4 a = ld_keep4(p, pol);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  }
+};
+template <>
+struct BlockRow<float, 2> {
+  __device__ static void load(const float* p, uint64_t pol, float (&v)[2]) {
+    const float2 a = ld_stream2(p, pol);
+    v[0] = a.x; v[1] = a.y;
+  }
+  __device__ static void load_x(const float* p, uint64_t pol, float (&v)[2]) {
+    const float2 a = ld_keep2(p, pol);
+    v[0] = a.x; v[1] = a.y;
+  }
+};
+
+template <typename T, typename Acc, int R, int C, bool VEC_X>
+__global__ void __launch_bounds__(256)
+    bcsr_rows(BcsrView B, const T* __restrict__ x, Acc* __restrict__ y) {
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t bi = gid / R;
+  const int r = static_cast<int>(gid % R);
+  if (bi >= B.mb) return;
+  const T* __restrict__ vals = static_cast<const T*>(B.values);
+  const uint64_t ps = policy_evict_first();
+  const uint64_t pk = policy_evict_last();
+  const int s = B.rowptr[bi];
+  const int e = B.rowptr[bi + 1];
+  Acc acc = Acc(0);
+#pragma unroll 2
+  for (int bp = s; bp < e; ++bp) {
+    const int bj = ld_stream(B.colind + bp, ps);
+    T v[C];
+    BlockRow<T, C>::load(vals + static_cast<int64_t>(bp) * (R * C) + r * C, ps, v);
+    const int gc0 = bj * C;
+    Acc part = Acc(0);
+    if (VEC_X && gc0 + C <= B.n) {
+      T xv[C];
+      BlockRow<T, C>::load_x(x + gc0, pk, xv);
+#pragma unroll
+      for (int c = 0; c < C; ++c) part = add_rn(part, prod<Acc>(v[c], xv[c]));
+    } else {
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        if (gc0 + c >= B.n) break;
+        part = add_rn(part, prod<Acc>(v[c], ld_keep(x + gc0 + c, pk)));
+      }
+    }
+    acc = add_rn(acc, part);
+  }
+  const int64_t gi = bi * R + r;
+  if (gi < B.m) y[gi] = acc;
+}
+
+}  // namespace spmvb

@@ -1,0 +1,207 @@
+// Host launchers for the SpMV kernels of one (T, Acc) pair. Included by the
+// three instantiation units spmv_f64f64.cu, spmv_f32f32.cu, spmv_f32f64.cu.
+// Launch shapes replace SpmvRunner::run's switch (src/cuda/spmv_cuda.cu:385-464).
+#pragma once
+
+#include <algorithm>
+
+#include "internal.hpp"
+#include "spmm_kernels.cuh"
+#include "spmv_kernels.cuh"
+
+namespace spmvb {
+
+constexpr int kScalarThreads = 256;
+constexpr int kScalarCap = 2048;
+constexpr int kRowThreads = 256;
+
+template <typename T, typename Acc, int G>
+static void launch_vector(const CsrView& v, int sms, const T* x, Acc* y,
+                          cudaStream_t s) {
+  const int64_t rows_per_block = (kRowThreads / kWarp) * (kWarp / G);
+  const int64_t need = (v.m + rows_per_block - 1) / rows_per_block;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(need, int64_t(sms) * 16)));
+  csr_vector<T, Acc, G><<<grid, kRowThreads, 0, s>>>(v, x, y);
+}
+
+template <typename T, typename Acc>
+spmvb_status launch_spmv(spmvb_matrix A, spmvb_kernel kernel, int lanes,
+                         int block, const T* x, Acc* y, cudaStream_t stream) {
+  const CsrView v = A->csr_view();
+  const int sms = A->ctx->sm_count;
+  if (A->m == 0) return SPMVB_OK;
+  switch (kernel) {
+    case SPMVB_CSR_SCALAR: {
+      const int tiles = (A->m + kScalarThreads - 1) / kScalarThreads;
+      csr_scalar_staged<T, Acc, kScalarThreads, kScalarCap>
+          <<<tiles, kScalarThreads, 0, stream>>>(v, x, y);
+      count_launch();
+      break;
+    }
+    case SPMVB_CSR_VECTOR: {
+      // Reference lane selection: 2/4/8/16, anything else -> 32
+      // (src/cuda/spmv_cuda.cu:394-420).
+      switch (lanes) {
+        case 2: launch_vector<T, Acc, 2>(v, sms, x, y, stream); break;
+        case 4: launch_vector<T, Acc, 4>(v, sms, x, y, stream); break;
+        case 8: launch_vector<T, Acc, 8>(v, sms, x, y, stream); break;
+        case 16: launch_vector<T, Acc, 16>(v, sms, x, y, stream); break;
+        default: launch_vector<T, Acc, 32>(v, sms, x, y, stream); break;
+      }
+      count_launch();
+      break;
+    }
+    case SPMVB_CSR_WARP:
+      launch_vector<T, Acc, 32>(v, sms, x, y, stream);
+      count_launch();
+      break;
+    case SPMVB_CSR_MERGE: {
+      SPMVB_TRY(build_merge(A));
+      MergeView mv;
+      mv.tile_row = A->merge_tile_row.as<int>();
+      mv.carry_row = A->merge_carry_row.as<int>();
+      mv.carry_val = A->merge_carry_val.get();
+      mv.num_items = static_cast<int64_t>(A->m) + A->nnz;
+      mv.num_tiles = A->merge_tiles;
+      mv.tile_items = kMergeTile;
+      csr_merge<T, Acc, kMergeThreads, kMergeIpt>
+          <<<mv.num_tiles, kMergeThreads, 0, stream>>>(v, mv, x, y);
+      merge_fixup<Acc><<<(mv.num_tiles + 255) / 256, 256, 0, stream>>>(mv, y);
+      count_launch(2);
+      break;
+    }
+    case SPMVB_ELL: {
+      SPMVB_TRY(build_ell(A));
+      EllView e;
+      e.colind = A->ell_colind.as<int>();
+      e.values = A->ell_values.get();
+      e.row_lengths = A->ell_rowlen.as<int>();
+      e.m = A->m;
+      e.n = A->n;
+      e.width = A->ell_width;
+      e.ld = A->m;
+      ell_rows<T, Acc, false><<<(A->m + kRowThreads - 1) / kRowThreads, kRowThreads, 0, stream>>>(e, x, y);
+      count_launch();
+      break;
+    }
+    case SPMVB_HYB: {
+      SPMVB_TRY(build_hyb(A, 0));
+      HybView h;
+      h.ell.colind = A->hyb_colind.as<int>();
+      h.ell.values = A->hyb_values.get();
+      h.ell.row_lengths = A->hyb_rowlen.as<int>();
+      h.ell.m = A->m;
+      h.ell.n = A->n;
+      h.ell.width = A->hyb_K;
+      h.ell.ld = A->m;
+      h.long_rows = A->hyb_long_rows.as<int>();
+      h.tail_ptr = A->hyb_tail_ptr.as<int>();
+      h.tail_colind = A->hyb_tail_colind.as<int>();
+      h.tail_values = A->hyb_tail_values.get();
+      h.n_long = A->hyb_n_long;
+      ell_rows<T, Acc, true><<<(A->m + kRowThreads - 1) / kRowThreads, kRowThreads, 0, stream>>>(h.ell, x, y);
+      count_launch();
+      if (h.n_long > 0) {
+        const int warps_per_block = kRowThreads / kWarp;
+        hyb_long_rows<T, Acc><<<(h.n_long + warps_per_block - 1) / warps_per_block, kRowThreads, 0, stream>>>(h, x, y);
+        count_launch();
+      }
+      break;
+    }
+    case SPMVB_BCSR: {
+      // Reference: block <= 2 -> 2x2, else 4x4 (src/cuda/spmv_cuda.cu:449-457).
+      const int bs = block <= 2 ? 2 : 4;
+      SPMVB_TRY(build_bcsr(A, bs));
+      const auto& b = bs == 2 ? A->bcsr2 : A->bcsr4;
+      BcsrView bv;
+      bv.rowptr = b.rowptr.as<int>();
+      bv.colind = b.colind.as<int>();
+      bv.values = b.values.get();
+      bv.m = A->m;
+      bv.n = A->n;
+      bv.R = bs;
+      bv.C = bs;
+      bv.mb = b.mb;
+      bv.block_nnz = b.block_nnz;
+      const bool vec_x = (reinterpret_cast<uintptr_t>(x) % 16) == 0;
+      const int64_t threads = int64_t(b.mb) * bs;
+      const int grid = static_cast<int>(std::max<int64_t>(1, (threads + kRowThreads - 1) / kRowThreads));
+      if (bs == 2) {
+        if (vec_x) bcsr_rows<T, Acc, 2, 2, true><<<grid, kRowThreads, 0, stream>>>(bv, x, y);
+        else bcsr_rows<T, Acc, 2, 2, false><<<grid, kRowThreads, 0, stream>>>(bv, x, y);
+      } else {
+        if (vec_x) bcsr_rows<T, Acc, 4, 4, true><<<grid, kRowThreads, 0, stream>>>(bv, x, y);
+        else bcsr_rows<T, Acc, 4, 4, false><<<grid, kRowThreads, 0, stream>>>(bv, x, y);
+      }
+      count_launch();
+      break;
+    }
+    default:
+      return fail(SPMVB_ERR_INVALID_ARGUMENT, "unknown SpMV kernel id " + std::to_string(int(kernel)));
+  }
+  SPMVB_TRY_CUDA(cudaGetLastError());
+  return SPMVB_OK;
+}
+
+// ---- SpMM ------------------------------------------------------------------
+template <typename T, typename Acc, int G, int W, bool VEC>
+static void launch_spmm_rows(const CsrView& v, const int* rows, int nrows,
+                             int sms, const T* X, Acc* Y, int k,
+                             cudaStream_t s) {
+  if (nrows <= 0) return;
+  const int64_t rows_per_block = (kRowThreads / kWarp) * (kWarp / G);
+  const int64_t need = (nrows + rows_per_block - 1) / rows_per_block;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(need, int64_t(sms) * 16)));
+  spmm_rows<T, Acc, G, W, VEC><<<grid, kRowThreads, 0, s>>>(v, rows, nrows, X, Y, k);
+  count_launch();
+}
+
+template <typename T, typename Acc, bool VEC>
+static void launch_spmm_tile(const CsrView& v, int tile, const int* rows,
+                             int nrows, int sms, const T* X, Acc* Y, int k,
+                             cudaStream_t s) {
+  constexpr int V = 16 / sizeof(T);
+  if constexpr (VEC) {
+    if (tile == 64) launch_spmm_rows<T, Acc, 64 / V, V, true>(v, rows, nrows, sms, X, Y, k, s);
+    else if (tile == 16) launch_spmm_rows<T, Acc, 16 / V, V, true>(v, rows, nrows, sms, X, Y, k, s);
+    else launch_spmm_rows<T, Acc, 32 / V, V, true>(v, rows, nrows, sms, X, Y, k, s);
+  } else {
+    if (tile == 64) launch_spmm_rows<T, Acc, 32, 2, false>(v, rows, nrows, sms, X, Y, k, s);
+    else if (tile == 16) launch_spmm_rows<T, Acc, 16, 1, false>(v, rows, nrows, sms, X, Y, k, s);
+    else launch_spmm_rows<T, Acc, 32, 1, false>(v, rows, nrows, sms, X, Y, k, s);
+  }
+}
+
+template <typename T, typename Acc>
+spmvb_status launch_spmm(spmvb_matrix A, int tile, int bucketed, int k,
+                         const T* X, Acc* Y, cudaStream_t stream) {
+  constexpr int V = 16 / sizeof(T);
+  if (A->m == 0 || k == 0) return SPMVB_OK;
+  const CsrView v = A->csr_view();
+  const int sms = A->ctx->sm_count;
+  // Reference tile selection: 16, 64, anything else -> 32 (src/cuda/spmm_cuda.cu:155-168).
+  const int t = (tile == 16 || tile == 64) ? tile : 32;
+  const bool vec = (k % V) == 0 && (reinterpret_cast<uintptr_t>(X) % 16) == 0;
+  if (!bucketed) {
+    if (vec) launch_spmm_tile<T, Acc, true>(v, t, nullptr, A->m, sms, X, Y, k, stream);
+    else launch_spmm_tile<T, Acc, false>(v, t, nullptr, A->m, sms, X, Y, k, stream);
+  } else {
+    SPMVB_TRY(build_buckets(A));
+    const int* rows = A->bucket_rows.as<int>();
+    const int n_sm = A->b_short + A->b_med;
+    if (vec) launch_spmm_tile<T, Acc, true>(v, t, rows, n_sm, sms, X, Y, k, stream);
+    else launch_spmm_tile<T, Acc, false>(v, t, rows, n_sm, sms, X, Y, k, stream);
+    if (A->b_long > 0) {
+      const int grid = std::min(A->b_long, sms * 8);
+      if (vec)
+        spmm_long_rows<T, Acc, V, true><<<grid, kRowThreads, 0, stream>>>(v, rows + n_sm, A->b_long, X, Y, k);
+      else
+        spmm_long_rows<T, Acc, 2, false><<<grid, kRowThreads, 0, stream>>>(v, rows + n_sm, A->b_long, X, Y, k);
+      count_launch();
+    }
+  }
+  SPMVB_TRY_CUDA(cudaGetLastError());
+  return SPMVB_OK;
+}
+
+}  // namespace spmvb

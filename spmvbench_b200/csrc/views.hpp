@@ -1,0 +1,87 @@
+// Trivially copyable device views of every storage format the kernels read.
+// They are the kernel arguments; the owning buffers live in the matrix handle
+// (matrix.hpp). Mirrors the role of DeviceCsr/DeviceEll/DeviceBcsr
+// (include/spmvbench/spmv_cuda.cuh:53-84), plus the hybrid, merge-path and
+// bucket views that have no reference counterpart.
+#pragma once
+
+#include <cstdint>
+
+namespace spmvb {
+
+// CSR. colind/values are padded with kPad zero entries past nnz so that
+// 16-byte vector loads that round a range up to a multiple of 4 entries stay
+// in bounds (padding column 0 is a valid index into x).
+constexpr int kPad = 64;
+
+struct CsrView {
+  const int* rowptr = nullptr;  // m + 1
+  const int* colind = nullptr;  // nnz + kPad
+  const void* values = nullptr; // nnz + kPad
+  int m = 0;
+  int n = 0;
+  int64_t nnz = 0;
+};
+
+// Column-major ELL: entry j of row i at j * ld + i. ld == m reproduces the
+// reference layout (src/formats.cpp:37-39).
+struct EllView {
+  const int* colind = nullptr;
+  const void* values = nullptr;
+  const int* row_lengths = nullptr;  // m
+  int m = 0;
+  int n = 0;
+  int width = 0;
+  int64_t ld = 0;
+};
+
+// Hybrid ELL(K) + CSR tail. Every row keeps its first min(len, K) entries in
+// the column-major ELL part; rows longer than K ("long rows") keep the rest
+// in a CSR tail indexed by long-row slot. The ELL kernel writes rows with
+// len <= K (hyb_len[i] >= 0); the long-row kernel writes the others.
+struct HybView {
+  EllView ell;                 // width K; row_lengths = len, or -1 for long rows
+  const int* long_rows = nullptr;   // n_long row ids, ascending
+  const int* tail_ptr = nullptr;    // n_long + 1 offsets into the tail
+  const int* tail_colind = nullptr; // + kPad
+  const void* tail_values = nullptr;
+  int n_long = 0;
+};
+
+// Blocked CSR with R x C row-major blocks (src/formats.cpp:45-105 layout).
+struct BcsrView {
+  const int* rowptr = nullptr;  // mb + 1
+  const int* colind = nullptr;  // block_nnz
+  const void* values = nullptr; // block_nnz * R * C
+  int m = 0;
+  int n = 0;
+  int R = 4;
+  int C = 4;
+  int mb = 0;
+  int64_t block_nnz = 0;
+};
+
+// Merge-path decomposition of the (m row ends) x (nnz entries) merge grid into
+// tiles of `tile_items` consecutive diagonals. tile_row[t] is the row
+// coordinate where tile t starts (tile_nz[t] = t*tile_items - tile_row[t]).
+// carry_row / carry_val are per-launch scratch: the partial sum a tile leaves
+// for a row that continues into the next tile (carry_row = -1: none).
+struct MergeView {
+  const int* tile_row = nullptr;  // num_tiles + 1
+  int* carry_row = nullptr;       // num_tiles
+  void* carry_val = nullptr;      // num_tiles, of the accumulator type
+  int64_t num_items = 0;          // m + nnz
+  int num_tiles = 0;
+  int tile_items = 0;
+};
+
+// Row-length buckets for SpMM (reference thresholds, src/cuda/spmm_cuda.cu:249-256):
+// rows[0, n_short) have <= 8 entries, the next n_med <= 64, the rest more.
+struct BucketView {
+  const int* rows = nullptr;
+  int n_short = 0;
+  int n_med = 0;
+  int n_long = 0;
+};
+
+}  // namespace spmvb

@@ -1,0 +1,132 @@
+"""Behaviour of the C ABI on the GPU: argument checks reject bad buffers
+before any kernel can touch them, the reference's clamping of lanes / block
+/ tile is kept, launches are counted, and the single-rank distributed path
+iterates exactly like the oracle."""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import spmvbench_b200 as S
+from gpu_util import assert_bitwise, oracle_y, run_spmv
+
+pytestmark = pytest.mark.gpu
+
+
+def small(ctx, dtype=S.F64):
+    A = S.generate(2, seed=71, scale_rows=1000)
+    return A, S.DeviceMatrix(ctx, A, dtype)
+
+
+def test_host_pointer_rejected(ctx):
+    A, M = small(ctx)
+    x_host = torch.zeros(A.n, dtype=torch.float64)  # CPU memory
+    y = torch.zeros(A.m, dtype=torch.float64, device="cuda")
+    with pytest.raises(S.SpmvbError) as e:
+        M.spmv(x_host, y)
+    assert e.value.status == 1 and "host memory" in str(e.value)
+
+
+def test_undersized_buffer_rejected(ctx):
+    A, M = small(ctx)
+    big = torch.zeros(1 << 23, dtype=torch.float64, device="cuda")  # 64 MiB allocation
+    x = torch.zeros(A.n, dtype=torch.float64, device="cuda")
+    tail = big[(1 << 23) - 10:]  # 10 entries before the end of the allocation
+    with pytest.raises(S.SpmvbError) as e:
+        M.spmv(x, tail)
+    assert e.value.status == 1 and "bytes" in str(e.value)
+
+
+def test_bad_arguments(ctx):
+    A, M = small(ctx)
+    x = torch.zeros(A.n, dtype=torch.float64, device="cuda")
+    y = torch.zeros(A.m, dtype=torch.float64, device="cuda")
+    with pytest.raises(S.SpmvbError) as e:
+        M.spmv(x, y, kernel=17)
+    assert e.value.status == 1
+    with pytest.raises(S.SpmvbError) as e:
+        M.spmv(x, y.float(), acc=S.F32)  # fp64 storage, fp32 accumulation
+    assert e.value.status == 3
+
+
+def test_reference_clamping_of_lanes_block_tile(ctx):
+    A, M = small(ctx)
+    x = S.generate_vector(72, A.n)
+    # lanes outside {2,4,8,16} -> 32 (src/cuda/spmv_cuda.cu:415-419)
+    assert_bitwise(run_spmv(M, x, S.CSR_VECTOR, lanes=32), run_spmv(M, x, S.CSR_VECTOR, lanes=7), "lanes")
+    # block <= 2 -> 2x2, else 4x4 (src/cuda/spmv_cuda.cu:449-457)
+    assert_bitwise(run_spmv(M, x, S.BCSR, block=2), run_spmv(M, x, S.BCSR, block=1), "block")
+    assert_bitwise(run_spmv(M, x, S.BCSR, block=4), run_spmv(M, x, S.BCSR, block=9), "block")
+    k = 8
+    B = torch.from_numpy(S.generate_vector(73, A.n * k).reshape(A.n, k)).cuda()
+    Y1 = torch.empty(A.m, k, dtype=torch.float64, device="cuda")
+    Y2 = torch.empty_like(Y1)
+    M.spmm(B, Y1, k, tile=32)
+    M.spmm(B, Y2, k, tile=48)  # anything else -> 32 (src/cuda/spmm_cuda.cu:155-168)
+    torch.cuda.synchronize()
+    assert torch.equal(Y1, Y2)
+
+
+def test_launch_count_and_info(ctx):
+    A, M = small(ctx)
+    x = S.generate_vector(74, A.n)
+    before = S.launch_count()
+    run_spmv(M, x, S.CSR_SCALAR)
+    assert S.launch_count() == before + 1
+    M.prepare(S.BCSR, 4)
+    info = M.info()
+    _, bci, _ = oracle.csr_to_bcsr(A.m, A.n, 4, A.rowptr, A.colind, A.values)
+    assert info["bcsr4_block_nnz"] == bci.size and info["bcsr2_block_nnz"] == -1
+    assert info["ell_padded_nnz"] == A.m * 16 and info["ell_touched_nnz"] == A.nnz
+    assert info["device_bytes"] > A.nnz * 12
+    g = S.query_gpu(0)
+    assert g["major"] >= 10 and g["sm_count"] > 0
+
+
+def test_single_rank_iteration_matches_oracle(ctx):
+    A = S.generate(2, seed=75, scale_rows=50000)
+    x0 = S.generate_vector(76, A.n)
+    bounds = S.partition_rows(A.rowptr, 1)
+    D = S.DistMatrix(ctx, 1, 0, None, A, bounds, S.F64)
+    D.set_x(x0)
+    D.iterate(3, kernel=S.CSR_SCALAR)
+    got = D.get_x()
+    x = x0
+    for _ in range(3):
+        x = oracle_y(A, x, S.F64, S.F64)
+    assert_bitwise(x, got, "iterated")
+    kms, sms = D.iterate_timed(2, kernel=S.CSR_SCALAR)
+    assert 0 < kms <= sms
+    D.close()
+
+
+_NEVER_JOINS = r"""
+import os, sys
+sys.path.insert(0, os.environ["SPMVB_ROOT"])
+import spmvbench_b200 as S
+ctx = S.Context(0)
+A = S.generate(2, seed=1, scale_rows=1000)
+b = S.partition_rows(A.rowptr, 2)
+try:
+    S.DistMatrix(ctx, 2, 0, S.nccl_unique_id(), A, b, S.F64)   # rank 1 never starts
+    print("NO-ERROR")
+except S.SpmvbError as e:
+    print("STATUS", e.status)
+"""
+
+
+def test_rank_that_never_joins_times_out(tmp_path):
+    """Failure detection on the host: communicator set-up is non-blocking and
+    bounded, so a missing peer gives SPMVB_ERR_TIMEOUT, not a hang. Only the
+    bootstrap waits; no collective is ever launched on the GPU."""
+    env = dict(os.environ, SPMVB_NCCL_INIT_TIMEOUT_S="5", NCCL_NVLS_ENABLE="0",
+               SPMVB_ROOT=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    out = subprocess.run([sys.executable, "-c", _NEVER_JOINS], env=env, capture_output=True, text=True,
+                         timeout=120)
+    assert "STATUS 7" in out.stdout, out.stdout + out.stderr

@@ -1,0 +1,186 @@
+"""SpMV parity on the GPU: every kernel, every (T, Acc) pair, against the
+oracle on the reference's golden matrices, its test-suite edge cases, and
+the seeded benchmark workloads (scaled and full size)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+import spmvbench_b200 as S
+from conftest import GOLDEN_NAMES, load_golden, mixed_x
+from gpu_util import (DTYPE_PAIRS, NP, assert_bitwise, assert_rows_within_bound, oracle_y, run_spmv)
+
+pytestmark = pytest.mark.gpu
+
+# (kernel, lanes, block, how it must match csr_omp): "exact" = bit for bit,
+# "bcsr" = bit for bit against spmv_bcsr_cpu and bounded against csr_omp,
+# "hyb" = bit for bit on rows held in the ELL part, bounded on long rows.
+VARIANTS = [(S.CSR_SCALAR, 1, 4, "exact")] + \
+           [(S.CSR_VECTOR, L, 4, "bound") for L in (2, 4, 8, 16, 32)] + \
+           [(S.CSR_WARP, 1, 4, "bound"), (S.CSR_MERGE, 1, 4, "bound"), (S.ELL, 1, 4, "exact"),
+            (S.HYB, 1, 4, "hyb"), (S.BCSR, 1, 2, "bcsr"), (S.BCSR, 1, 4, "bcsr")]
+
+
+def golden_csr(name):
+    g = load_golden(name)
+    return g, S.CsrMatrix(int(g["m"]), int(g["n"]), g["rowptr"], g["colind"], g["values"])
+
+
+def check_variant(ctx, A, x, dtype, acc, kernel, lanes, block, how, label, M=None):
+    M = M or S.DeviceMatrix(ctx, A, dtype)
+    got = run_spmv(M, x, kernel, lanes, block, acc)
+    ref = oracle_y(A, x, dtype, acc)
+    tag = f"{label} {S.kernel_name(kernel)} lanes={lanes} block={block} dtype={dtype}/{acc}"
+    if how == "exact":
+        assert_bitwise(ref, got, tag)
+    elif how == "bcsr":
+        vals = np.ascontiguousarray(A.values, NP[dtype])
+        brp, bci, bva = oracle.csr_to_bcsr(A.m, A.n, block, A.rowptr, A.colind, vals)
+        yb = oracle.spmv_bcsr(A.m, A.n, block, block, brp, bci, bva, np.ascontiguousarray(x, NP[dtype]), NP[acc])
+        assert_bitwise(yb, got, tag + " vs spmv_bcsr_cpu")
+        assert_rows_within_bound(A, x, ref, got, dtype, acc, tag)
+    elif how == "hyb":
+        K = M.info()["hyb_width"]
+        short = np.diff(A.rowptr) <= K
+        assert_bitwise(ref[short], got[short], tag + " (ELL rows)")
+        assert_rows_within_bound(A, x, ref, got, dtype, acc, tag)
+    else:
+        assert_rows_within_bound(A, x, ref, got, dtype, acc, tag)
+    return M
+
+
+@pytest.mark.parametrize("name", GOLDEN_NAMES)
+@pytest.mark.parametrize("dtype,acc", DTYPE_PAIRS)
+def test_golden_all_kernels(ctx, name, dtype, acc):
+    g, A = golden_csr(name)
+    M = S.DeviceMatrix(ctx, A, dtype)
+    for x in (g["x"], mixed_x(A.n)):
+        for kernel, lanes, block, how in VARIANTS:
+            check_variant(ctx, A, x, dtype, acc, kernel, lanes, block, how, name, M)
+    if dtype == S.F64 and acc == S.F64:
+        # csr_omp's own output on the fixture x is reproduced bit for bit
+        assert_bitwise(g["y_dd"], run_spmv(M, g["x"], S.CSR_SCALAR), name)
+        assert_bitwise(g["y_ell_dd"], run_spmv(M, g["x"], S.ELL), name)
+        assert_bitwise(g["y_bcsr4_dd"], run_spmv(M, g["x"], S.BCSR, block=4), name)
+        assert_bitwise(g["y_bcsr2_dd"], run_spmv(M, g["x"], S.BCSR, block=2), name)
+    if dtype == S.F32 and acc == S.F32:
+        assert_bitwise(g["y_ff"], run_spmv(M, g["x"], S.CSR_SCALAR), name)
+    if dtype == S.F32 and acc == S.F64:
+        assert_bitwise(g["y_fd"], run_spmv(M, g["x"], S.CSR_SCALAR, acc=S.F64), name)
+
+
+WORKLOADS_SCALED = [(1, 0), (2, 200000), (3, 200000), (4, 100000)]
+
+
+@pytest.mark.parametrize("which,rows", WORKLOADS_SCALED)
+@pytest.mark.parametrize("dtype,acc", DTYPE_PAIRS)
+def test_workloads_all_kernels(ctx, which, rows, dtype, acc):
+    A = S.generate(which, seed=31, scale_rows=rows)
+    x = S.generate_vector(32, A.n)
+    M = S.DeviceMatrix(ctx, A, dtype)
+    for kernel, lanes, block, how in VARIANTS:
+        if kernel == S.ELL and which == 3:
+            continue  # covered by test_ell_refuses_infeasible_padding
+        check_variant(ctx, A, x, dtype, acc, kernel, lanes, block, how, f"w{which}", M)
+
+
+def test_full_size_uniform_fp64(ctx):
+    A = S.generate(2, seed=41)
+    x = S.generate_vector(42, A.n)
+    M = S.DeviceMatrix(ctx, A, S.F64)
+    ref = oracle_y(A, x, S.F64, S.F64)
+    assert_bitwise(ref, run_spmv(M, x, S.CSR_SCALAR), "C2 scalar")
+    assert_bitwise(ref, run_spmv(M, x, S.ELL), "C2 ell")
+    for k, lanes in ((S.CSR_MERGE, 1), (S.CSR_VECTOR, 8), (S.CSR_VECTOR, 16), (S.CSR_WARP, 1), (S.HYB, 1)):
+        assert_rows_within_bound(A, x, ref, run_spmv(M, x, k, lanes), S.F64, S.F64, S.kernel_name(k))
+
+
+def test_full_size_powerlaw_fp64(ctx):
+    A = S.generate(3, seed=43)
+    x = S.generate_vector(44, A.n)
+    M = S.DeviceMatrix(ctx, A, S.F64)
+    ref = oracle_y(A, x, S.F64, S.F64)
+    assert_bitwise(ref, run_spmv(M, x, S.CSR_SCALAR), "C3 scalar")
+    for k, lanes in ((S.CSR_MERGE, 1), (S.HYB, 1), (S.CSR_WARP, 1), (S.CSR_VECTOR, 4)):
+        assert_rows_within_bound(A, x, ref, run_spmv(M, x, k, lanes), S.F64, S.F64, S.kernel_name(k))
+
+
+def test_full_size_blocks_fp64(ctx):
+    A = S.generate(4, seed=45)
+    x = S.generate_vector(46, A.n)
+    M = S.DeviceMatrix(ctx, A, S.F64)
+    check_variant(ctx, A, x, S.F64, S.F64, S.BCSR, 1, 4, "bcsr", "C4", M)
+    assert_bitwise(oracle_y(A, x, S.F64, S.F64), run_spmv(M, x, S.CSR_SCALAR), "C4 scalar")
+    assert M.info()["bcsr4_block_nnz"] == 125000 * 8
+
+
+def test_ell_refuses_infeasible_padding(ctx):
+    # 1M rows x a 50,000-entry row = 5e10 padded slots (~600 GB): the
+    # reference's eager ELL cannot run this matrix; here it is a clear error.
+    A = S.generate(3, seed=47)
+    M = S.DeviceMatrix(ctx, A, S.F64)
+    with pytest.raises(S.SpmvbError) as e:
+        M.prepare(S.ELL)
+    assert e.value.status == 3 and "hybrid" in str(e.value)
+
+
+@pytest.mark.parametrize("which,rows", [(2, 50000), (3, 100000), (4, 20000), (1, 0)])
+def test_device_formats_match_reference_layout(ctx, which, rows):
+    A = S.generate(which, seed=51, scale_rows=rows)
+    M = S.DeviceMatrix(ctx, A, S.F64)
+    if which != 3:
+        w, ecol, ev, rl = M.export_ell()
+        ow, ocol, ov, orl = oracle.csr_to_ell(A.m, A.rowptr, A.colind, A.values)
+        assert w == ow
+        assert_bitwise(ocol, ecol, "ell colind")
+        assert_bitwise(ov, ev, "ell values")
+        assert_bitwise(orl, rl, "row_lengths")
+    for b in (2, 4):
+        rp, ci, va = M.export_bcsr(b)
+        orp, oci, ova = oracle.csr_to_bcsr(A.m, A.n, b, A.rowptr, A.colind, A.values)
+        assert_bitwise(orp, rp, f"bcsr{b} rowptr")
+        assert_bitwise(oci, ci, f"bcsr{b} colind")
+        assert_bitwise(ova, va, f"bcsr{b} values")
+
+
+@pytest.mark.parametrize("name", GOLDEN_NAMES)
+def test_golden_formats_match_reference(ctx, name):
+    g, A = golden_csr(name)
+    M = S.DeviceMatrix(ctx, A, S.F64)
+    w, ecol, ev, rl = M.export_ell()
+    assert w == int(g["ell_width"])
+    assert_bitwise(g["ell_colind"], ecol, "ell colind")
+    assert_bitwise(g["ell_values"], ev, "ell values")
+    assert_bitwise(g["ell_row_lengths"], rl, "row_lengths")
+    for b in (2, 4):
+        rp, ci, va = M.export_bcsr(b)
+        assert_bitwise(g[f"bcsr{b}_rowptr"], rp, "bcsr rowptr")
+        assert_bitwise(g[f"bcsr{b}_colind"], ci, "bcsr colind")
+        assert_bitwise(g[f"bcsr{b}_values"], va, "bcsr values")
+
+
+def test_merge_is_deterministic(ctx):
+    A = S.generate(3, seed=53, scale_rows=300000)
+    x = S.generate_vector(54, A.n)
+    M = S.DeviceMatrix(ctx, A, S.F64)
+    a = run_spmv(M, x, S.CSR_MERGE)
+    for _ in range(3):
+        assert_bitwise(a, run_spmv(M, x, S.CSR_MERGE), "merge rerun")
+
+
+def test_empty_shapes(ctx):
+    for m, n in ((0, 5), (5, 0), (1, 1)):
+        A = S.CsrMatrix(m, n, np.zeros(m + 1, np.int32), np.zeros(0, np.int32), np.zeros(0))
+        M = S.DeviceMatrix(ctx, A, S.F64)
+        for kernel, lanes, block, _ in VARIANTS:
+            got = run_spmv(M, np.zeros(n), kernel, lanes, block)
+            assert got.shape == (m,) and np.all(got == 0.0)
+
+
+def test_host_buffer_entry_point_matches_device(ctx):
+    A = S.generate(2, seed=55, scale_rows=100000)
+    x = S.generate_vector(56, A.n)
+    M = S.DeviceMatrix(ctx, A, S.F64)
+    for kernel in (S.CSR_SCALAR, S.CSR_MERGE, S.ELL):
+        assert_bitwise(run_spmv(M, x, kernel), M.spmv_host(x, kernel=kernel), "host entry")

@@ -1,0 +1,233 @@
+"""Host-side logic of libspmvb through its C ABI, on the CPU: the library
+loads and exports every entry point include/spmvb.h declares; validation,
+statistics, kernel selection, partitioning, sharding and the seeded
+generators behave as specified. No kernel is launched here."""
+from __future__ import annotations
+
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+import oracle
+import spmvbench_b200 as S
+from conftest import GOLDEN_NAMES, ROOT, load_golden
+from spmvbench_b200 import _lib
+
+
+def header_functions():
+    text = open(os.path.join(ROOT, "include", "spmvb.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(spmvb_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = S.load()
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True,
+                         check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if line.split()}
+    declared = header_functions()
+    assert len(declared) >= 30
+    missing = [f for f in declared if f not in exported]
+    assert not missing, missing
+    for f in declared:
+        assert hasattr(lib, f)
+    assert set(_lib.SIGNATURES) <= set(declared)
+
+
+def test_status_strings_and_version():
+    lib = S.load()
+    assert b"sm_100a" in lib.spmvb_version()
+    for code, text in _lib.STATUS.items():
+        assert lib.spmvb_status_string(code).decode() == text
+    assert S.kernel_name(S.HYB) == "hyb" and S.kernel_name(99) == "unknown"
+    assert [S.kernel_name(i) for i in range(7)] == _lib.KERNEL_NAMES
+
+
+@pytest.mark.skipif(S.gpu_available(), reason="a GPU is present")
+def test_no_device_is_reported_not_crashed():
+    with pytest.raises(S.SpmvbError) as e:
+        S.Context(0)
+    assert e.value.status == 8
+
+
+# ---- validation ------------------------------------------------------------------
+def _bad(rowptr, colind, m, n):
+    return S.CsrMatrix(m, n, np.array(rowptr, np.int32), np.array(colind, np.int32), np.ones(len(colind)))
+
+
+@pytest.mark.parametrize("A,what", [
+    (_bad([1, 2], [0, 0], 1, 2), "rowptr[0]"),
+    (_bad([0, 2, 1], [0, 1], 2, 2), "decreases"),
+    (_bad([0, 1, 2], [0, 2], 2, 2), "out of range"),
+    (_bad([0, 1, 2], [0, -1], 2, 2), "out of range"),
+])
+def test_validation_rejects_bad_csr(A, what):
+    with pytest.raises(S.SpmvbError) as e:
+        S.csr_validate(A)
+    assert e.value.status == 2 and what in str(e.value)
+
+
+def test_validation_rejects_nnz_mismatch():
+    A = S.CsrMatrix(2, 2, np.array([0, 1, 2], np.int32), np.array([0, 1], np.int32), np.ones(2))
+    lib = S.load()
+    rp = np.array([0, 1, 3], np.int32)
+    st = lib.spmvb_csr_validate(2, 2, 2, rp.ctypes.data, A.colind.ctypes.data, None)
+    assert st == 2 and b"nnz" in lib.spmvb_last_error()
+
+
+@pytest.mark.parametrize("name", GOLDEN_NAMES)
+def test_validation_accepts_golden(name):
+    g = load_golden(name)
+    A = S.CsrMatrix(int(g["m"]), int(g["n"]), g["rowptr"], g["colind"], g["values"])
+    assert S.csr_validate(A) == (int(np.diff(g["rowptr"]).max()) if A.m else 0)
+
+
+# ---- statistics / selection -----------------------------------------------------------
+FIELDS = oracle.STAT_FIELDS
+
+
+def _check_stats(A):
+    mine = S.row_stats(A, histogram=True)
+    ref = oracle.row_stats(A.m, A.n, A.rowptr, A.colind if A.nnz else None)
+    for f in FIELDS:
+        assert mine[f] == ref[f], f
+    np.testing.assert_array_equal(mine["row_nnz_histogram"], ref["row_nnz_histogram"])
+    return mine
+
+
+@pytest.mark.parametrize("name", GOLDEN_NAMES)
+def test_row_stats_bitwise_golden(name):
+    g = load_golden(name)
+    A = S.CsrMatrix(int(g["m"]), int(g["n"]), g["rowptr"], g["colind"], g["values"])
+    mine = _check_stats(A)
+    np.testing.assert_array_equal(np.array([mine[f] for f in FIELDS]), g["stats"])
+    ch = S.choose_spmv_reference(mine)
+    assert [ch["kernel"], ch["lanes"], ch["block_r"], ch["block_c"]] == g["choice"].tolist()
+
+
+@pytest.mark.parametrize("which,rows", [(1, 0), (2, 50000), (3, 0), (4, 40000)])
+def test_row_stats_bitwise_workloads(which, rows):
+    A = S.generate(which, seed=3, scale_rows=rows)
+    st = _check_stats(A)
+    if which == 4:  # every stored 4x4 block is dense
+        assert st["dense_share_of_stored_4x4"] == 1.0
+
+
+def test_choose_reference_rules_match_oracle_grid():
+    rng = np.random.default_rng(0)
+    for _ in range(2000):
+        st = dict(nnz=int(rng.choice([1000, 49999, 50000, 10 ** 6])), mean_row_nnz=float(rng.uniform(0, 80)),
+                  cv_row_nnz=float(rng.uniform(0, 3)), max_over_mean=float(rng.uniform(1, 100)),
+                  ell_padding_overhead=float(rng.uniform(1, 3)), frac_dense_blocks_4x4=float(rng.uniform(0, 1)))
+        a = S.choose_spmv_reference(st)
+        b = oracle.choose_spmv(st)
+        assert [a[k] for k in ("kernel", "lanes", "block_r", "block_c", "rule")] == \
+               [b[k] for k in ("kernel", "lanes", "block_r", "block_c", "rule")]
+        assert a["reason"]
+
+
+def test_choose_b200_rules():
+    assert S.choose_spmv(dict(nnz=10 ** 7, mean_row_nnz=5, cv_row_nnz=30, max_over_mean=9000))["name"] == "csr_merge"
+    assert S.choose_spmv(dict(nnz=10 ** 7, mean_row_nnz=32, cv_row_nnz=0,
+                              dense_share_of_stored_4x4=1.0))["name"] == "bcsr"
+    assert S.choose_spmv(dict(nnz=10 ** 7, mean_row_nnz=16, cv_row_nnz=0))["name"] == "csr_scalar"
+    assert S.choose_spmv(dict(nnz=10 ** 7, mean_row_nnz=9, cv_row_nnz=0.01))["name"] == "csr_scalar"
+    c = S.choose_spmv(dict(nnz=10 ** 7, mean_row_nnz=200, cv_row_nnz=0.1))
+    assert c["name"] == "csr_vector" and c["lanes"] == 32
+
+
+# ---- partitioning / sharding ---------------------------------------------------------------
+def _partition_rule(rowptr, parts):
+    """bounds[g] = lower_bound(rowptr, ceil(g*nnz/parts))."""
+    m = rowptr.size - 1
+    nnz = int(rowptr[-1])
+    b = [0] + [int(np.searchsorted(rowptr, -(-g * nnz // parts), side="left")) for g in range(1, parts)] + [m]
+    return np.maximum.accumulate(np.minimum(np.array(b), m)).astype(np.int32)
+
+
+@pytest.mark.parametrize("which,rows", [(2, 30000), (3, 0), (1, 0)])
+@pytest.mark.parametrize("parts", [1, 2, 3, 4, 8])
+def test_partition_rule_and_balance(which, rows, parts):
+    A = S.generate(which, seed=5, scale_rows=rows)
+    b = S.partition_rows(A.rowptr, parts)
+    np.testing.assert_array_equal(b, _partition_rule(A.rowptr, parts))
+    assert b[0] == 0 and b[-1] == A.m and np.all(np.diff(b) >= 0)
+    share = np.diff(A.rowptr[b])
+    maxrow = int(np.diff(A.rowptr).max())
+    assert share.max() <= -(-A.nnz // parts) + maxrow
+
+
+def test_partition_edge_cases():
+    rp = np.array([0, 0, 0], np.int32)  # all-empty rows
+    assert S.partition_rows(rp, 4).tolist() == [0, 0, 0, 0, 2]
+    rp = np.array([0, 100], np.int32)  # one heavy row, more parts than rows
+    assert S.partition_rows(rp, 3).tolist() == [0, 1, 1, 1]
+
+
+@pytest.mark.parametrize("parts", [1, 2, 4, 8])
+def test_shard_renumbering_round_trip(parts):
+    A = S.generate(3, seed=9, scale_rows=20000)
+    b = S.partition_rows(A.rowptr, parts)
+    for r in range(parts):
+        mr, rp, ci = S.shard_csr(A, b, r)
+        assert mr == int(np.diff(b).max())
+        p0, p1 = A.rowptr[b[r]], A.rowptr[b[r + 1]]
+        np.testing.assert_array_equal(rp, A.rowptr[b[r]:b[r + 1] + 1] - p0)
+        owner, local = ci // mr, ci % mr
+        np.testing.assert_array_equal(b[owner] + local, A.colind[p0:p1])
+        assert np.all(local < (b[owner + 1] - b[owner]))
+
+
+# ---- generators ---------------------------------------------------------------------
+def test_generators_shapes_and_structure():
+    A1 = S.generate(1)
+    assert (A1.m, A1.n, A1.nnz) == (100000, 100000, 899980)
+    lens = np.diff(A1.rowptr)
+    assert lens.min() == 5 and lens.max() == 9
+    diag = A1.values[A1.colind == np.repeat(np.arange(A1.m), lens)]
+    assert diag.size == A1.m and diag.min() > 9.0 and diag.max() < 11.0
+    A2 = S.generate(2, scale_rows=40000)
+    assert A2.nnz == 16 * 40000 and np.all(np.diff(A2.rowptr) == 16)
+    c = A2.colind.reshape(-1, 16)
+    assert np.all(np.diff(c, axis=1) > 0) and c.min() >= 0 and c.max() < A2.n
+    assert np.abs(A2.values).max() < 1.0
+    A4 = S.generate(4, scale_rows=40000)
+    assert A4.nnz == 32 * 40000 and np.all(np.diff(A4.rowptr) == 32)
+    c4 = A4.colind.reshape(-1, 8, 4)
+    assert np.all(c4 % 4 == np.arange(4)) and np.all(np.diff(c4[:, :, 0], axis=1) > 0)
+    # the 4 rows of a block row share the block columns
+    assert np.all(c4.reshape(-1, 4, 8, 4)[:, :, :, 0] == c4.reshape(-1, 4, 8, 4)[:, :1, :, 0])
+
+
+def test_powerlaw_generator_distribution():
+    A3 = S.generate(3)
+    lens = np.diff(A3.rowptr)
+    assert A3.m == 1_000_000 and lens.min() >= 1 and lens.max() <= 50000
+    # Zipf(2.1): P(len=1) = 1/zeta(2.1) ~ 0.641; mean of the clipped law ~ 5
+    assert abs((lens == 1).mean() - 0.641) < 0.005
+    assert 4.0 < lens.mean() < 6.5
+    for i in np.flatnonzero(lens > 1000)[:5]:
+        c = A3.colind[A3.rowptr[i]:A3.rowptr[i + 1]]
+        assert np.all(np.diff(c) > 0)
+
+
+def test_generators_are_deterministic():
+    a = S.generate(3, seed=11, scale_rows=5000)
+    b = S.generate(3, seed=11, scale_rows=5000)
+    c = S.generate(3, seed=12, scale_rows=5000)
+    for f in ("rowptr", "colind", "values"):
+        np.testing.assert_array_equal(getattr(a, f), getattr(b, f))
+    assert a.nnz != c.nnz or not np.array_equal(a.colind, c.colind)
+    x = S.generate_vector(4, 1000)
+    np.testing.assert_array_equal(x, S.generate_vector(4, 1000))
+    assert np.abs(x).max() < 1.0 and abs(x.mean()) < 0.1
+
+
+def test_generator_rejects_bad_arguments():
+    with pytest.raises(S.SpmvbError):
+        S.generate(9)
+    with pytest.raises(S.SpmvbError):
+        S.generate(2, scale_rows=8)
