@@ -76,6 +76,14 @@ __device__ __forceinline__ void stage_products(
       c[g] = ok[g] ? ld_stream4(colind + c0 + q, pol_stream)
                    : make_int4(0, 0, 0, 0);
     }
+    // Values do not depend on the column indices: issue them before the
+    // x gathers so they are in flight while colind returns.
+    T av[GROUPS][4];
+#pragma unroll
+    for (int g = 0; g < GROUPS; ++g) {
+      const int q = base + (g * NT + static_cast<int>(threadIdx.x)) * 4;
+      if (ok[g]) ld_stream_quad(vals + c0 + q, pol_stream, av[g]);
+    }
     T xv[GROUPS][4];
 #pragma unroll
     for (int g = 0; g < GROUPS; ++g) {
@@ -85,12 +93,6 @@ __device__ __forceinline__ void stage_products(
         xv[g][2] = ld_keep(x + c[g].z, pol_keep);
         xv[g][3] = ld_keep(x + c[g].w, pol_keep);
       }
-    }
-    T av[GROUPS][4];
-#pragma unroll
-    for (int g = 0; g < GROUPS; ++g) {
-      const int q = base + (g * NT + static_cast<int>(threadIdx.x)) * 4;
-      if (ok[g]) ld_stream_quad(vals + c0 + q, pol_stream, av[g]);
     }
 #pragma unroll
     for (int g = 0; g < GROUPS; ++g) {
