@@ -147,6 +147,15 @@ spmvb_status spmvb_query_gpu(int device, spmvb_gpu_info* out);
  * reference's SpmvRunner relies on (src/cuda/spmv_cuda.cu:233-290). */
 spmvb_status spmvb_context_create(int device, spmvb_context* out);
 spmvb_status spmvb_context_destroy(spmvb_context ctx);
+/* Synchronizes the device and reports whether any kernel launched through
+ * this context gave up a bounded wait since the last check
+ * (SPMVB_ERR_TIMEOUT; the word is then cleared). The host-buffer entry
+ * points perform this check on their own stream before returning. */
+spmvb_status spmvb_context_check(spmvb_context ctx);
+/* Launches a kernel whose bounded wait can never be satisfied (an mbarrier
+ * expecting bytes no copy delivers), with a short limit, to exercise the
+ * failure path; expect SPMVB_ERR_TIMEOUT. Nothing is left in flight. */
+spmvb_status spmvb_selftest_wait_timeout(spmvb_context ctx);
 
 /* ---- matrices ------------------------------------------------------------ */
 /* Validate a host CSR (rowptr[0]==0, non-decreasing, rowptr[m]==nnz, every

@@ -195,6 +195,10 @@ class Context:
         self.handle = h
         self.device = device
 
+    def check(self) -> None:
+        """Synchronize and raise if a kernel gave up a bounded wait."""
+        call("spmvb_context_check", self.handle)
+
     def close(self):
         if self.handle:
             load().spmvb_context_destroy(self.handle)

@@ -79,6 +79,8 @@ SIGNATURES = {
     "spmvb_query_gpu": (C.c_int, [C.c_int, C.POINTER(GpuInfo)]),
     "spmvb_context_create": (C.c_int, [C.c_int, C.POINTER(P)]),
     "spmvb_context_destroy": (C.c_int, [P]),
+    "spmvb_context_check": (C.c_int, [P]),
+    "spmvb_selftest_wait_timeout": (C.c_int, [P]),
     "spmvb_matrix_create_csr": (C.c_int, [P, C.c_int, C.c_int32, C.c_int32, C.c_int64,
                                           P, P, P, C.POINTER(P)]),
     "spmvb_matrix_destroy": (C.c_int, [P]),

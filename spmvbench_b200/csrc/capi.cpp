@@ -121,7 +121,7 @@ int64_t spmvb_matrix_st::device_bytes() const {
   b += hyb_colind.bytes() + hyb_values.bytes() + hyb_rowlen.bytes() + hyb_long_rows.bytes() +
        hyb_tail_ptr.bytes() + hyb_tail_colind.bytes() + hyb_tail_values.bytes();
   for (const auto* B : {&bcsr2, &bcsr4}) b += B->rowptr.bytes() + B->colind.bytes() + B->values.bytes();
-  b += merge_tile_row.bytes() + merge_carry_row.bytes() + merge_carry_val.bytes();
+  b += tma_rows.bytes() + merge_tile_row.bytes() + merge_carry_row.bytes() + merge_carry_val.bytes();
   b += bucket_rows.bytes() + stage_in.bytes() + stage_out.bytes();
   return b;
 }
@@ -197,13 +197,31 @@ spmvb_status spmvb_context_create(int device, spmvb_context* out) {
   SPMVB_TRY_CUDA(cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device));
   SPMVB_TRY_CUDA(cudaDeviceGetAttribute(&c->l2_bytes, cudaDevAttrL2CacheSize, device));
   SPMVB_TRY_CUDA(cudaDeviceGetAttribute(&c->max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+  SPMVB_TRY(c->err.alloc(16));
   *out = c.release();
   return SPMVB_OK;
 }
 
 spmvb_status spmvb_context_destroy(spmvb_context ctx) {
   clear_error();
-  delete ctx;
+  if (ctx) {
+    DeviceGuard g(ctx->device);
+    delete ctx;
+  }
+  return SPMVB_OK;
+}
+
+spmvb_status spmvb_context_check(spmvb_context ctx) {
+  clear_error();
+  if (!ctx) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null context");
+  DeviceGuard g(ctx->device);
+  SPMVB_TRY_CUDA(cudaDeviceSynchronize());
+  int code = 0;
+  SPMVB_TRY_CUDA(cudaMemcpy(&code, ctx->err.get(), sizeof(int), cudaMemcpyDeviceToHost));
+  if (code != 0) {
+    SPMVB_TRY_CUDA(cudaMemset(ctx->err.get(), 0, sizeof(int)));
+    return fail(SPMVB_ERR_TIMEOUT, "a kernel's bounded wait gave up (device error code " + std::to_string(code) + ")");
+  }
   return SPMVB_OK;
 }
 
@@ -277,7 +295,7 @@ spmvb_status spmvb_matrix_prepare(spmvb_matrix A, spmvb_kernel kernel, int param
   clear_error();
   if (!A) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null matrix");
   switch (kernel) {
-    case SPMVB_CSR_SCALAR:
+    case SPMVB_CSR_SCALAR: return build_tma(A);
     case SPMVB_CSR_VECTOR:
     case SPMVB_CSR_WARP: return SPMVB_OK;
     case SPMVB_CSR_MERGE: return build_merge(A);
@@ -339,6 +357,18 @@ spmvb_status spmvb_matrix_export_bcsr(spmvb_matrix A, int block, int32_t* h_rowp
   return SPMVB_OK;
 }
 
+// Reads the context's device error word after `s` has been synchronized.
+static spmvb_status check_err_word(spmvb_context ctx, cudaStream_t s) {
+  int code = 0;
+  SPMVB_TRY_CUDA(cudaMemcpyAsync(&code, ctx->err.get(), sizeof(int), cudaMemcpyDeviceToHost, s));
+  SPMVB_TRY_CUDA(cudaStreamSynchronize(s));
+  if (code != 0) {
+    SPMVB_TRY_CUDA(cudaMemsetAsync(ctx->err.get(), 0, sizeof(int), s));
+    return fail(SPMVB_ERR_TIMEOUT, "a kernel's bounded wait gave up (device error code " + std::to_string(code) + ")");
+  }
+  return SPMVB_OK;
+}
+
 static spmvb_status check_pair(spmvb_matrix A, spmvb_dtype acc) {
   if (!A) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null matrix");
   if (acc != SPMVB_F32 && acc != SPMVB_F64) return fail(SPMVB_ERR_INVALID_ARGUMENT, "bad accumulator dtype");
@@ -391,7 +421,7 @@ spmvb_status spmvb_spmv_host(spmvb_matrix A, spmvb_kernel kernel, int lanes, int
   SPMVB_TRY(dispatch_spmv(A, kernel, lanes, block, A->stage_in.get(), A->stage_out.get(), acc, s));
   if (yb) SPMVB_TRY_CUDA(cudaMemcpyAsync(h_y, A->stage_out.get(), yb, cudaMemcpyDeviceToHost, s));
   SPMVB_TRY_CUDA(cudaStreamSynchronize(s));
-  return SPMVB_OK;
+  return check_err_word(A->ctx, s);
 }
 
 spmvb_status spmvb_spmm(spmvb_matrix A, int tile, int bucketed, int k, const void* d_X, void* d_Y, spmvb_dtype acc,

@@ -92,6 +92,9 @@ struct spmvb_context_st {
   int sm_count = 0;
   int l2_bytes = 0;
   int max_smem_optin = 0;
+  // Device error word: kernels whose bounded waits give up write a non-zero
+  // code here (see spmvb_context_check).
+  spmvb::DevBuf err;
 };
 
 struct spmvb_matrix_st {
@@ -132,6 +135,11 @@ struct spmvb_matrix_st {
     spmvb::DevBuf rowptr, colind, values;
   } bcsr2, bcsr4;
 
+  // Persistent-kernel row ranges (nnz-balanced, kPersistPerSm CTAs per SM)
+  bool tma_built = false;
+  int tma_grid = 0;
+  spmvb::DevBuf tma_rows;
+
   // Merge-path partition + carry scratch (sized for the widest accumulator)
   bool merge_built = false;
   int merge_tiles = 0;
@@ -168,6 +176,10 @@ spmvb_status build_hyb(spmvb_matrix A, int forced_k);
 spmvb_status build_bcsr(spmvb_matrix A, int block);
 spmvb_status build_merge(spmvb_matrix A);
 spmvb_status build_buckets(spmvb_matrix A);
+spmvb_status build_tma(spmvb_matrix A);
+
+// CTAs per SM of the persistent TMA-pipelined CSR kernel.
+constexpr int kPersistPerSm = 2;
 
 // Merge-path tile shape shared by the partition builder and the kernel.
 constexpr int kMergeThreads = 256;

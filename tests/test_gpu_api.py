@@ -106,6 +106,20 @@ def test_single_rank_iteration_matches_oracle(ctx):
     D.close()
 
 
+def test_bounded_wait_reports_timeout(ctx):
+    """Failure detection on the GPU: a wait that nothing will satisfy gives up
+    after its limit, the kernel records it, and the host gets
+    SPMVB_ERR_TIMEOUT; the context stays usable afterwards."""
+    lib = S.load()
+    assert lib.spmvb_selftest_wait_timeout(ctx.handle) == 7
+    assert b"bounded wait" in lib.spmvb_last_error()
+    ctx.check()  # the error word was cleared
+    A, M = small(ctx)
+    x = S.generate_vector(77, A.n)
+    assert_bitwise(oracle_y(A, x, S.F64, S.F64), run_spmv(M, x, S.CSR_SCALAR), "after timeout")
+    ctx.check()
+
+
 _NEVER_JOINS = r"""
 import os, sys
 sys.path.insert(0, os.environ["SPMVB_ROOT"])
