@@ -211,6 +211,27 @@ spmvb_status spmvb_spmv_host(spmvb_matrix A, spmvb_kernel kernel, int lanes,
                              int block, const void* h_x, void* h_y,
                              spmvb_dtype acc, void* stream);
 
+/* Merge-path y = A x that allocates nothing. No counterpart in the reference.
+ * For callers that cannot call cudaMalloc: device memory owned by another
+ * allocator (a caching allocator or a pool sized at start-up), or latency
+ * rules that forbid allocation after start-up (cudaMalloc/cudaFree may
+ * synchronize the device). The caller owns every array on the device: a
+ * valid CSR (rowptr m+1, colind/values nnz, as spmvb_csr_validate checks), x
+ * (n entries of dtype) and y (m entries of acc); the current device is used.
+ * Scratch lives in a fixed 1,048,832-byte __device__ array held by every GPU
+ * that loads the library until exit, which bounds m + nnz to 117,440,512
+ * (65,536 merge tiles of 1,792 items); larger requests fail with
+ * SPMVB_ERR_UNSUPPORTED. The first call on a device looks the array up
+ * (cudaGetSymbolAddress), so make it before any stream capture. Calls share
+ * the array: calls that overlap on the GPU race; calls ordered on one stream
+ * do not. Each call writes all the scratch it reads, so nothing is cleared. */
+spmvb_status spmvb_spmv_merge_noalloc(spmvb_dtype dtype, int32_t m, int32_t n,
+                                      int64_t nnz, const int32_t* d_rowptr,
+                                      const int32_t* d_colind,
+                                      const void* d_values, const void* d_x,
+                                      void* d_y, spmvb_dtype acc,
+                                      void* stream);
+
 /* ---- SpMM ------------------------------------------------------------------ */
 /* Y (m x k, row-major, acc) = A X (n x k, row-major, matrix dtype).
  * tile in {16,32,64}: columns of Y a row group covers per pass; bucketed != 0
