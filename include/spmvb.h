@@ -247,6 +247,14 @@ spmvb_status spmvb_spmm_host(spmvb_matrix A, int tile, int bucketed, int k,
                              const void* h_X, void* h_Y, spmvb_dtype acc,
                              void* stream);
 
+/* Measures this device's random-gather ceiling: 8-byte loads at random
+ * positions of an L2-resident vector of n doubles (`gathers` of them, in
+ * one launch, best of 6 after 2 warm-up launches). SpMV on matrices whose
+ * column indices have no locality is bounded by this rate, not by HBM
+ * bandwidth. No reference counterpart (its roofline is HBM only). */
+spmvb_status spmvb_probe_gather_rate(spmvb_context ctx, int64_t n,
+                                     int64_t gathers, double* gathers_per_s);
+
 /* ---- statistics and kernel selection ---------------------------------------- */
 /* Replaces compute_row_stats (include/spmvbench/stats.hpp:44-52). histogram
  * (optional) receives max_row_nnz+1 counts when hist_cap is large enough;

@@ -195,6 +195,13 @@ class Context:
         self.handle = h
         self.device = device
 
+    def gather_rate(self, n: int = 1_000_000, gathers: int = 16_000_000) -> float:
+        """Measured random 8-byte gathers per second from an L2-resident
+        vector of n doubles (the ceiling of locality-free SpMV)."""
+        r = C.c_double()
+        call("spmvb_probe_gather_rate", self.handle, n, gathers, C.byref(r))
+        return r.value
+
     def check(self) -> None:
         """Synchronize and raise if a kernel gave up a bounded wait."""
         call("spmvb_context_check", self.handle)

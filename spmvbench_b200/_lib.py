@@ -96,6 +96,7 @@ SIGNATURES = {
                                            C.c_int, P]),
     "spmvb_spmm": (C.c_int, [P, C.c_int, C.c_int, C.c_int, P, P, C.c_int, P]),
     "spmvb_spmm_host": (C.c_int, [P, C.c_int, C.c_int, C.c_int, P, P, C.c_int, P]),
+    "spmvb_probe_gather_rate": (C.c_int, [P, C.c_int64, C.c_int64, C.POINTER(C.c_double)]),
     "spmvb_compute_row_stats": (C.c_int, [P, P, C.c_int32, C.c_int32, C.c_int64,
                                           C.POINTER(RowStats), P, C.c_int64]),
     "spmvb_choose_spmv": (C.c_int, [C.POINTER(RowStats), C.POINTER(Choice)]),

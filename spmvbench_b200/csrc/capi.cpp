@@ -295,7 +295,7 @@ spmvb_status spmvb_matrix_prepare(spmvb_matrix A, spmvb_kernel kernel, int param
   clear_error();
   if (!A) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null matrix");
   switch (kernel) {
-    case SPMVB_CSR_SCALAR: return build_tma(A);
+    case SPMVB_CSR_SCALAR:
     case SPMVB_CSR_VECTOR:
     case SPMVB_CSR_WARP: return SPMVB_OK;
     case SPMVB_CSR_MERGE: return build_merge(A);

@@ -153,6 +153,96 @@ __global__ void __launch_bounds__(NT)
 }
 
 // ---------------------------------------------------------------------------
+// CSR scalar, warp-staged: the kernel behind SPMVB_CSR_SCALAR.
+//
+// On B200 the random x gathers, not the matrix stream, bound short-row SpMV:
+// 16M random 8-byte gathers from an L2-resident x take ~62 us on their own.
+// What matters is how many independent gathers each SM keeps in flight, so
+// this kernel has no CTA-wide barrier at all. Each warp owns 32 consecutive
+// rows; their entries are one contiguous range of the CSR arrays, which the
+// warp reads in chunks of CH entries with 16-byte vector loads (lane l takes
+// entries 4l..4l+3 of every 128-entry block, so each load instruction covers
+// 512 contiguous bytes), issuing every gather of the chunk before forming any
+// product. Products go to the warp's own slice of shared memory; after a
+// __syncwarp each lane adds its row's products in order, carrying the running
+// sum across chunks, so every row is summed left to right from zero exactly
+// as csr_omp sums it. Rows of any length work (long rows simply span chunks).
+// ---------------------------------------------------------------------------
+template <typename T, typename Acc, int CH>
+__global__ void __launch_bounds__(256)
+    csr_scalar_warp(CsrView A, const T* __restrict__ x, Acc* __restrict__ y) {
+  constexpr int WARPS = 8;
+  constexpr int GROUPS = CH / (kWarp * 4);  // groups of 4 entries per lane per chunk
+  static_assert(CH % (kWarp * 4) == 0, "CH must be a multiple of 128");
+  constexpr int SLOT = swz_size<Acc>(CH);
+  __shared__ Acc s_prod_all[WARPS * SLOT];
+  const int lane = threadIdx.x & (kWarp - 1);
+  const int wib = threadIdx.x / kWarp;
+  Acc* s_prod = s_prod_all + wib * SLOT;
+  const T* __restrict__ vals = static_cast<const T*>(A.values);
+  const uint64_t ps = policy_evict_first();
+  const uint64_t pk = policy_evict_last();
+  const int64_t warp = static_cast<int64_t>(blockIdx.x) * WARPS + wib;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * WARPS;
+  for (int64_t r0 = warp * kWarp; r0 < A.m; r0 += nwarps * kWarp) {
+    const int64_t row = r0 + lane;
+    const bool live = row < A.m;
+    const int64_t last = (A.m - r0 < kWarp) ? A.m - r0 - 1 : kWarp - 1;
+    int64_t rs = 0, re = 0;
+    if (live) {
+      rs = A.rowptr[row];
+      re = A.rowptr[row + 1];
+    }
+    const int64_t P0 = __shfl_sync(0xffffffffu, rs, 0);
+    const int64_t P1 = __shfl_sync(0xffffffffu, re, static_cast<int>(last));
+    Acc sum = Acc(0);
+    for (int64_t c0 = P0 & ~int64_t(3); c0 < P1; c0 += CH) {
+      const int span = static_cast<int>((P1 - c0) < CH ? (P1 - c0) : CH);
+      int4 c[GROUPS];
+      T av[GROUPS][4];
+      T xv[GROUPS][4];
+#pragma unroll
+      for (int g = 0; g < GROUPS; ++g) {
+        const int q = (g * kWarp + lane) * 4;
+        c[g] = q < span ? ld_stream4(A.colind + c0 + q, ps) : make_int4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int g = 0; g < GROUPS; ++g) {
+        const int q = (g * kWarp + lane) * 4;
+        if (q < span) ld_stream_quad(vals + c0 + q, ps, av[g]);
+      }
+#pragma unroll
+      for (int g = 0; g < GROUPS; ++g) {
+        const int q = (g * kWarp + lane) * 4;
+        if (q < span) {
+          xv[g][0] = ld_keep(x + c[g].x, pk);
+          xv[g][1] = ld_keep(x + c[g].y, pk);
+          xv[g][2] = ld_keep(x + c[g].z, pk);
+          xv[g][3] = ld_keep(x + c[g].w, pk);
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < GROUPS; ++g) {
+        const int q = (g * kWarp + lane) * 4;
+        if (q < span) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) s_prod[swz<Acc>(q + i)] = prod<Acc>(av[g][i], xv[g][i]);
+        }
+      }
+      __syncwarp();
+      if (live) {
+        const int64_t c1 = c0 + span;
+        const int a = static_cast<int>((rs > c0 ? rs : c0) - c0);
+        const int b = static_cast<int>((re < c1 ? re : c1) - c0);
+        for (int q = a; q < b; ++q) sum = add_rn(sum, s_prod[swz<Acc>(q)]);
+      }
+      __syncwarp();
+    }
+    if (live) y[row] = sum;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // CSR scalar, TMA-pipelined (the B200 form of the kernel above).
 //
 // Persistent CTAs, each owning a contiguous, nnz-balanced range of rows

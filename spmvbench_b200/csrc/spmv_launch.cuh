@@ -18,6 +18,8 @@ constexpr int kRowThreads = 256;
 constexpr int kTmaThreads = 256;
 constexpr int kTmaChunk = 2048;
 constexpr int kTmaStages = 3;
+// Warp-staged scalar kernel: entries per warp chunk.
+constexpr int kScalarWarpChunk = 512;
 
 template <typename T, typename Acc>
 static spmvb_status launch_scalar_tma(spmvb_matrix A, const T* x, Acc* y, cudaStream_t stream) {
@@ -51,9 +53,14 @@ spmvb_status launch_spmv(spmvb_matrix A, spmvb_kernel kernel, int lanes,
   const int sms = A->ctx->sm_count;
   if (A->m == 0) return SPMVB_OK;
   switch (kernel) {
-    case SPMVB_CSR_SCALAR:
-      SPMVB_TRY((launch_scalar_tma<T, Acc>(A, x, y, stream)));
+    case SPMVB_CSR_SCALAR: {
+      const int64_t groups = (int64_t(A->m) + kWarp - 1) / kWarp;  // 32 rows per warp
+      const int64_t need = (groups + 7) / 8;
+      const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(need, int64_t(sms) * 16)));
+      csr_scalar_warp<T, Acc, kScalarWarpChunk><<<grid, 256, 0, stream>>>(v, x, y);
+      count_launch();
       break;
+    }
     case SPMVB_CSR_VECTOR: {
       // Reference lane selection: 2/4/8/16, anything else -> 32
       // (src/cuda/spmv_cuda.cu:394-420).

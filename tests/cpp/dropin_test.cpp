@@ -111,8 +111,12 @@ static void gpu_tests() {
   std::uniform_int_distribution<int> col(0, n - 1);
   std::uniform_real_distribution<double> val(-1.0, 1.0), e(-6.0, 6.0), bit(0.0, 1.0);
   std::vector<std::vector<std::pair<int, double>>> rows(m);
-  for (int i = 0; i < m; ++i)
-    for (int j = 0; j < per + (i % 7); ++j) rows[i].push_back({col(rng), val(rng)});
+  // distinct columns per row (base + j*4729 mod n, gcd(4729, n) = 1): BCSR
+  // keeps only the last of repeated (row, column) entries, CSR sums them
+  for (int i = 0; i < m; ++i) {
+    const int base = col(rng);
+    for (int j = 0; j < per + (i % 7); ++j) rows[i].push_back({(base + j * 4729) % n, val(rng)});
+  }
   const auto A = make_csr(m, n, rows);
   std::vector<double> x(n);
   for (auto& v : x) v = (bit(rng) < 0.5 ? -1.0 : 1.0) * std::pow(10.0, e(rng));
