@@ -14,6 +14,10 @@ matrix). The kernel is the one the B200 heuristic picks for the matrix.
 Extra objects on the same line:
   roofline      HBM roofline of the SpMV kernel (algorithmic bytes per launch
                 / CUDA-event launch time, over MEASURED_PEAKS.json hbm_gbs)
+  gather_roofline  the same launches against the device's random-gather
+                ceiling (one 8-byte x gather per entry; the ceiling is
+                measured live by spmvb_probe_gather_rate): on a matrix with
+                random columns this, not HBM, is the binding limit
   cpu_baseline  the reference's own csr_omp (oracle/_ref, compiled from the
                 reference sources; the C restatement if that is absent) on
                 the same matrix, all host threads, rank 0 at N=1
@@ -73,6 +77,18 @@ def spmv_bytes(m, n, nnz, vbytes=8, ibytes=4, ybytes=8):
     """Compulsory traffic of CSR SpMV: values + colind + rowptr + x + y once
     (the reference's bw_lo model, bench/bench_main.cpp:449-457)."""
     return nnz * (vbytes + ibytes) + (m + 1) * ibytes + n * vbytes + m * ybytes
+
+
+def kernel_bytes(S, kernel, M, m, n, nnz):
+    """Compulsory bytes of the format `kernel` reads: ELL/HYB read row_lengths
+    (m ints) instead of rowptr (bench/bench_main.cpp:661-667); BCSR its
+    blocks (bench/bench_main.cpp:668-678)."""
+    if kernel in (S.ELL, S.HYB):
+        return nnz * 12 + m * 4 + n * 8 + m * 8
+    if kernel == S.BCSR:
+        bn = M.info()["bcsr4_block_nnz"]
+        return bn * (16 * 8 + 4) + ((m + 3) // 4 + 1) * 4 + n * 8 + m * 8
+    return spmv_bytes(m, n, nnz)
 
 
 def measured_peak():
@@ -289,20 +305,26 @@ def main():
     ev1.record(stream)
     ev1.synchronize()
     launches = S.launch_count() - launches0
+    if world > 1:
+        lt = torch.tensor([launches], dtype=torch.int64, device="cuda")
+        dist.all_reduce(lt)
+        launches = int(lt.item())
     barrier()
     clocks = sampler.stop() if rank == 0 else None
     ms_rank = ev0.elapsed_time(ev1) / args.steps
     ms = max_over_ranks(ms_rank)
     gflops = world * 2.0 * A.nnz / (ms * 1e-3) / 1e9
 
-    bytes_launch = spmv_bytes(A.m, A.n, A.nnz)
+    bytes_launch = kernel_bytes(S, kernel, M, A.m, A.n, A.nnz)
     peak, peak_src = measured_peak()
     achieved = bytes_launch / (ms * 1e-3) / 1e9
-    kname = {S.CSR_SCALAR: "csr_scalar_staged", S.CSR_MERGE: "csr_merge", S.CSR_VECTOR: "csr_vector",
+    kname = {S.CSR_SCALAR: "csr_scalar_warp", S.CSR_MERGE: "csr_merge", S.CSR_VECTOR: "csr_vector",
              S.CSR_WARP: "csr_vector", S.ELL: "ell_rows", S.HYB: "ell_rows", S.BCSR: "bcsr_rows"}[kernel]
 
-    # parity spot check of this rank's result (host reference from the oracle is
-    # not used here; the kernel's own contract is tested in tests/)
+    # Second roofline: the device's random-gather ceiling (one 8-byte gather
+    # per entry from the L2-resident x), measured live on this GPU.
+    gather_peak = ctx.gather_rate(A.n, A.nnz)
+    gathers_achieved = A.nnz / (ms * 1e-3)
     # ---- e2e through the host-buffer entry point ----
     xp = torch.from_numpy(xh.copy()).pin_memory()
     yp = torch.empty(A.m, dtype=torch.float64).pin_memory()
@@ -386,6 +408,9 @@ def main():
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": peak_src,
                          "traffic": traffic, "kernel": kname},
+            "gather_roofline": {"achieved": gathers_achieved, "peak": gather_peak, "unit": "gathers/s",
+                                "frac": gathers_achieved / gather_peak,
+                                "peak_source": "measured live (spmvb_probe_gather_rate)"},
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks,
             "spmm_k64": spmm, "iterated": iterated,
         }

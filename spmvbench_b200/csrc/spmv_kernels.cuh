@@ -729,7 +729,7 @@ struct BlockRow<float, 2> {
   }
 };
 
-template <typename T, typename Acc, int R, int C, bool VEC_X>
+template <typename T, typename Acc, int R, int C, bool VEC_X, int UB>
 __global__ void __launch_bounds__(256)
     bcsr_rows(BcsrView B, const T* __restrict__ x, Acc* __restrict__ y) {
   const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -742,26 +742,42 @@ __global__ void __launch_bounds__(256)
   const int s = B.rowptr[bi];
   const int e = B.rowptr[bi + 1];
   Acc acc = Acc(0);
-#pragma unroll 2
-  for (int bp = s; bp < e; ++bp) {
-    const int bj = ld_stream(B.colind + bp, ps);
-    T v[C];
-    BlockRow<T, C>::load(vals + static_cast<int64_t>(bp) * (R * C) + r * C, ps, v);
-    const int gc0 = bj * C;
-    Acc part = Acc(0);
-    if (VEC_X && gc0 + C <= B.n) {
-      T xv[C];
-      BlockRow<T, C>::load_x(x + gc0, pk, xv);
+  // UB blocks per batch: all their indices, block rows and x slices are
+  // requested before any product is formed.
+  for (int bp0 = s; bp0 < e; bp0 += UB) {
+    int bj[UB];
+    T v[UB][C];
+    T xv[UB][C];
 #pragma unroll
-      for (int c = 0; c < C; ++c) part = add_rn(part, prod<Acc>(v[c], xv[c]));
-    } else {
+    for (int u = 0; u < UB; ++u) bj[u] = (bp0 + u < e) ? ld_stream(B.colind + bp0 + u, ps) : 0;
 #pragma unroll
-      for (int c = 0; c < C; ++c) {
-        if (gc0 + c >= B.n) break;
-        part = add_rn(part, prod<Acc>(v[c], ld_keep(x + gc0 + c, pk)));
+    for (int u = 0; u < UB; ++u)
+      if (bp0 + u < e) BlockRow<T, C>::load(vals + static_cast<int64_t>(bp0 + u) * (R * C) + r * C, ps, v[u]);
+#pragma unroll
+    for (int u = 0; u < UB; ++u) {
+      const int gc0 = bj[u] * C;
+      if (bp0 + u < e) {
+        if (VEC_X && gc0 + C <= B.n) {
+          BlockRow<T, C>::load_x(x + gc0, pk, xv[u]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < C; ++c) xv[u][c] = (gc0 + c < B.n) ? ld_keep(x + gc0 + c, pk) : T(0);
+        }
       }
     }
-    acc = add_rn(acc, part);
+#pragma unroll
+    for (int u = 0; u < UB; ++u) {
+      if (bp0 + u < e) {
+        const int gc0 = bj[u] * C;
+        Acc part = Acc(0);
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+          if (gc0 + c >= B.n) break;  // trailing partial block column
+          part = add_rn(part, prod<Acc>(v[u][c], xv[u][c]));
+        }
+        acc = add_rn(acc, part);
+      }
+    }
   }
   const int64_t gi = bi * R + r;
   if (gi < B.m) y[gi] = acc;

@@ -18,6 +18,8 @@ constexpr int kRowThreads = 256;
 constexpr int kTmaThreads = 256;
 constexpr int kTmaChunk = 2048;
 constexpr int kTmaStages = 3;
+// BCSR: blocks requested per batch per thread.
+constexpr int kBcsrBatch = 4;
 // Warp-staged scalar kernel: entries per warp chunk.
 constexpr int kScalarWarpChunk = 512;
 
@@ -150,11 +152,11 @@ spmvb_status launch_spmv(spmvb_matrix A, spmvb_kernel kernel, int lanes,
       const int64_t threads = int64_t(b.mb) * bs;
       const int grid = static_cast<int>(std::max<int64_t>(1, (threads + kRowThreads - 1) / kRowThreads));
       if (bs == 2) {
-        if (vec_x) bcsr_rows<T, Acc, 2, 2, true><<<grid, kRowThreads, 0, stream>>>(bv, x, y);
-        else bcsr_rows<T, Acc, 2, 2, false><<<grid, kRowThreads, 0, stream>>>(bv, x, y);
+        if (vec_x) bcsr_rows<T, Acc, 2, 2, true, kBcsrBatch><<<grid, kRowThreads, 0, stream>>>(bv, x, y);
+        else bcsr_rows<T, Acc, 2, 2, false, kBcsrBatch><<<grid, kRowThreads, 0, stream>>>(bv, x, y);
       } else {
-        if (vec_x) bcsr_rows<T, Acc, 4, 4, true><<<grid, kRowThreads, 0, stream>>>(bv, x, y);
-        else bcsr_rows<T, Acc, 4, 4, false><<<grid, kRowThreads, 0, stream>>>(bv, x, y);
+        if (vec_x) bcsr_rows<T, Acc, 4, 4, true, kBcsrBatch><<<grid, kRowThreads, 0, stream>>>(bv, x, y);
+        else bcsr_rows<T, Acc, 4, 4, false, kBcsrBatch><<<grid, kRowThreads, 0, stream>>>(bv, x, y);
       }
       count_launch();
       break;

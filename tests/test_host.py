@@ -133,9 +133,10 @@ def test_choose_b200_rules():
     assert S.choose_spmv(dict(nnz=10 ** 7, mean_row_nnz=5, cv_row_nnz=30, max_over_mean=9000))["name"] == "csr_merge"
     assert S.choose_spmv(dict(nnz=10 ** 7, mean_row_nnz=32, cv_row_nnz=0,
                               dense_share_of_stored_4x4=1.0))["name"] == "bcsr"
-    assert S.choose_spmv(dict(nnz=10 ** 7, mean_row_nnz=16, cv_row_nnz=0))["name"] == "csr_scalar"
-    assert S.choose_spmv(dict(nnz=10 ** 7, mean_row_nnz=9, cv_row_nnz=0.01))["name"] == "csr_scalar"
-    c = S.choose_spmv(dict(nnz=10 ** 7, mean_row_nnz=200, cv_row_nnz=0.1))
+    assert S.choose_spmv(dict(nnz=10 ** 7, mean_row_nnz=16, cv_row_nnz=0, ell_padding_overhead=1.0))["name"] == "ell"
+    assert S.choose_spmv(dict(nnz=10 ** 7, mean_row_nnz=9, cv_row_nnz=0.01, ell_padding_overhead=1.1))["name"] == "ell"
+    assert S.choose_spmv(dict(nnz=10 ** 7, mean_row_nnz=9, cv_row_nnz=0.9, ell_padding_overhead=4))["name"] == "csr_merge"
+    c = S.choose_spmv(dict(nnz=10 ** 7, mean_row_nnz=200, cv_row_nnz=0.1, ell_padding_overhead=3))
     assert c["name"] == "csr_vector" and c["lanes"] == 32
 
 
