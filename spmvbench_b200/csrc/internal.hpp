@@ -182,8 +182,8 @@ spmvb_status build_tma(spmvb_matrix A);
 constexpr int kPersistPerSm = 2;
 
 // Merge-path tile shape shared by the partition builder and the kernel.
-constexpr int kMergeThreads = 256;
-constexpr int kMergeIpt = 7;
+constexpr int kMergeThreads = 128;
+constexpr int kMergeIpt = 11;
 constexpr int kMergeTile = kMergeThreads * kMergeIpt;
 
 // Device launchers, one instantiation per (T, Acc) in spmv_<t><acc>.cu.

@@ -32,7 +32,12 @@
 
 namespace spmvb {
 
-// Tiles of kMergeTile merge items; the scratch holds, per tile, its start row
+// Merge-path tile of this entry point: 256 threads x 7 items.
+constexpr int kNoallocThreads = 256;
+constexpr int kNoallocIpt = 7;
+constexpr int kNoallocTile = kNoallocThreads * kNoallocIpt;
+
+// Tiles of kNoallocTile merge items; the scratch holds, per tile, its start row
 // (plus one), its carry row and its carry value (8 bytes, the widest Acc),
 // each region starting on a 256-byte boundary.
 constexpr int kNoallocMaxTiles = 65536;
@@ -172,9 +177,9 @@ void launch_noalloc(const CsrView& v, unsigned char* scratch, int tiles, const T
   mv.carry_val = scratch + kNoallocCarryValOffset;
   mv.num_items = static_cast<int64_t>(v.m) + v.nnz;
   mv.num_tiles = tiles;
-  mv.tile_items = kMergeTile;
-  merge_partition<<<(tiles + 1 + 255) / 256, 256, 0, s>>>(v, mv.num_items, kMergeTile, tiles, tile_row);
-  csr_merge_scratch<T, Acc, kMergeThreads, kMergeIpt><<<tiles, kMergeThreads, 0, s>>>(v, mv, x, y);
+  mv.tile_items = kNoallocTile;
+  merge_partition<<<(tiles + 1 + 255) / 256, 256, 0, s>>>(v, mv.num_items, kNoallocTile, tiles, tile_row);
+  csr_merge_scratch<T, Acc, kNoallocThreads, kNoallocIpt><<<tiles, kNoallocThreads, 0, s>>>(v, mv, x, y);
   merge_fixup<Acc><<<(tiles + 255) / 256, 256, 0, s>>>(mv, y);
   count_launch(3);
 }
@@ -196,11 +201,11 @@ extern "C" spmvb_status spmvb_spmv_merge_noalloc(spmvb_dtype dtype, int32_t m, i
   if (m < 0 || n < 0 || nnz < 0 || nnz > INT32_MAX) return fail(SPMVB_ERR_INVALID_ARGUMENT, "bad m, n or nnz");
   if (m == 0) return SPMVB_OK;
   const int64_t items = static_cast<int64_t>(m) + nnz;
-  const int64_t tiles = (items + kMergeTile - 1) / kMergeTile;
+  const int64_t tiles = (items + kNoallocTile - 1) / kNoallocTile;
   if (tiles > kNoallocMaxTiles) {
     return fail(SPMVB_ERR_UNSUPPORTED,
                 "m + nnz = " + std::to_string(items) + " exceeds the no-allocation limit of " +
-                    std::to_string(static_cast<int64_t>(kNoallocMaxTiles) * kMergeTile) +
+                    std::to_string(static_cast<int64_t>(kNoallocMaxTiles) * kNoallocTile) +
                     " (its scratch is a fixed " + std::to_string(kNoallocScratchBytes) + "-byte device array)");
   }
   if (!d_rowptr || (nnz > 0 && (!d_colind || !d_values)) || (n > 0 && !d_x) || !d_y)

@@ -19,7 +19,7 @@ constexpr int kTmaThreads = 256;
 constexpr int kTmaChunk = 2048;
 constexpr int kTmaStages = 3;
 // BCSR: blocks requested per batch per thread.
-constexpr int kBcsrBatch = 4;
+constexpr int kBcsrBatch = 2;
 // Warp-staged scalar kernel: entries per warp chunk.
 constexpr int kScalarWarpChunk = 512;
 

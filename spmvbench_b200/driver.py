@@ -1,0 +1,262 @@
+"""Command-line driver, the B200 counterpart of SpMVBench's `bench`
+(bench/bench_main.cpp:957-984):
+
+    python -m spmvbench_b200.driver --stats    [--workload W ...]
+    python -m spmvbench_b200.driver --auto     [--workload W ...] [--dtype f64|f32]
+    python -m spmvbench_b200.driver --bench    [--workload W ...] [--dtype ...] [--iters N]
+    python -m spmvbench_b200.driver --validate [--workload W ...]
+    python -m spmvbench_b200.driver --profile KERNEL --workload W [--steps N] [--warmup N]
+
+Workloads are the seeded benchmark matrices (1 banded, 2 uniform, 3 power-law,
+4 4x4 blocks; see spmvbench_b200.WORKLOADS) instead of .mtx files.
+
+--stats    row statistics (compute_row_stats fields, bench_main.cpp:102-139)
+--auto     choose_spmv's pick against every kernel measured on the device; a
+           hit is a pick within 1.1x of the fastest (the reference counts exact
+           hits only, bench_main.cpp:229-253); writes results/heuristic.csv
+--bench    every kernel: median/min over CUDA-event-timed launches, GFLOP/s,
+           compulsory-traffic GB/s and fraction of the measured HBM peak, and
+           the random-gather ceiling; writes results/bench.csv
+--validate every kernel against the bit-exact csr_scalar result of the same
+           launch inputs: kernels that keep csr_omp's order must match bit for
+           bit, the others must stay within 2*gamma_n*sum|a_ij x_j| per row
+--profile  warmup + steps launches of one kernel on one workload (for ncu)
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import json
+import os
+import statistics
+import sys
+
+import numpy as np
+
+from . import (BCSR, CSR_MERGE, CSR_SCALAR, CSR_VECTOR, CSR_WARP, ELL, F32, F64, HYB, WORKLOADS,
+               Context, DeviceMatrix, choose_spmv, generate, generate_vector, kernel_name, row_stats)
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+# (label, kernel id, lanes, block) - the variants the reference's bench times
+# (bench_main.cpp:651-658), plus every lane count, 2x2 blocks and HYB.
+VARIANTS = [("csr_scalar", CSR_SCALAR, 1, 4)] + \
+           [(f"csr_vector_l{L}", CSR_VECTOR, L, 4) for L in (2, 4, 8, 16, 32)] + \
+           [("csr_warp", CSR_WARP, 1, 4), ("csr_merge", CSR_MERGE, 1, 4), ("ell", ELL, 1, 4),
+            ("hyb", HYB, 1, 4), ("bcsr_2x2", BCSR, 1, 2), ("bcsr_4x4", BCSR, 1, 4)]
+EXACT = {CSR_SCALAR, ELL}  # kernels that keep csr_omp's summation order
+
+
+def _peak_gbs():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return float(json.load(open(p))["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def _bytes(kernel, block, M, A, es):
+    m, n, nnz = A.m, A.n, A.nnz
+    if kernel in (ELL, HYB):
+        return nnz * (es + 4) + m * 4 + n * es + m * es
+    if kernel == BCSR:
+        info = M.info()
+        bn = info["bcsr2_block_nnz" if block <= 2 else "bcsr4_block_nnz"]
+        b = 2 if block <= 2 else 4
+        return bn * (b * b * es + 4) + ((m + b - 1) // b + 1) * 4 + n * es + m * es
+    return nnz * (es + 4) + (m + 1) * 4 + n * es + m * es
+
+
+def _time(M, x, y, kernel, lanes, block, iters, warmup):
+    import torch
+    s = torch.cuda.current_stream()
+    for _ in range(warmup):
+        M.spmv(x, y, kernel=kernel, lanes=lanes, block=block, stream=s)
+    torch.cuda.synchronize()
+    samples = []
+    for _ in range(iters):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(s)
+        M.spmv(x, y, kernel=kernel, lanes=lanes, block=block, stream=s)
+        b.record(s)
+        b.synchronize()
+        samples.append(a.elapsed_time(b))
+    return statistics.median(samples), min(samples)
+
+
+def _setup(which, dtype, seed=2024):
+    import torch
+    A = generate(which, seed=seed)
+    xh = generate_vector(999, A.n)
+    npd = np.float64 if dtype == F64 else np.float32
+    ctx = Context(0)
+    M = DeviceMatrix(ctx, A, dtype)
+    x = torch.from_numpy(xh.astype(npd)).cuda()
+    y = torch.empty(A.m, dtype=torch.float64 if dtype == F64 else torch.float32, device="cuda")
+    return ctx, A, M, x, y, xh
+
+
+def _usable(M, kernel, block):
+    try:
+        M.prepare(kernel, block if kernel == BCSR else 0)
+        return True
+    except Exception as e:  # noqa: BLE001 - an unsupported format is reported, not fatal
+        print(f"  {kernel_name(kernel)}: {e}")
+        return False
+
+
+def cmd_stats(args):
+    for w in args.workload:
+        A = generate(w)
+        s = row_stats(A)
+        print(f"=== {WORKLOADS[w]} ===")
+        print("  " + ", ".join(f"{k}={v:.6g}" if isinstance(v, float) else f"{k}={v}" for k, v in s.items()))
+    return 0
+
+
+def _measure_all(which, dtype, iters, warmup):
+    ctx, A, M, x, y, _ = _setup(which, dtype)
+    es = 8 if dtype == F64 else 4
+    rows = []
+    for label, k, lanes, block in VARIANTS:
+        if k == BCSR and which == 3:
+            continue  # 1M block rows x 50,000-entry rows: blocks would not be the format
+        if not _usable(M, k, block):
+            continue
+        med, mn = _time(M, x, y, k, lanes, block, iters, warmup)
+        rows.append(dict(kernel=label, id=k, lanes=lanes, block=block, median_ms=med, min_ms=mn,
+                         gflops=2 * A.nnz / (med * 1e-3) / 1e9, gbs=_bytes(k, block, M, A, es) / (med * 1e-3) / 1e9))
+    gather = ctx.gather_rate(A.n, A.nnz)
+    return A, rows, gather
+
+
+def cmd_auto(args):
+    dtype = F64 if args.dtype == "f64" else F32
+    out = []
+    for w in args.workload:
+        A, rows, _ = _measure_all(w, dtype, args.iters, args.warmup)
+        st = row_stats(A)
+        c = choose_spmv(st)
+        best = min(rows, key=lambda r: r["median_ms"])
+        pick = [r for r in rows if r["id"] == c["kernel"] and (c["kernel"] != CSR_VECTOR or r["lanes"] == c["lanes"])
+                and (c["kernel"] != BCSR or r["block"] == c["block_r"])]
+        chosen_ms = pick[0]["median_ms"] if pick else float("nan")
+        slow = chosen_ms / best["median_ms"]
+        out.append(dict(matrix=WORKLOADS[w], chosen=c["name"], oracle_best=best["kernel"], chosen_ms=chosen_ms,
+                        best_ms=best["median_ms"], hit=int(slow <= 1.1), slowdown=slow, reason=c["reason"]))
+        print(f"{WORKLOADS[w]:24s} chosen={c['name']:12s} best={best['kernel']:14s} "
+              f"chosen_ms={chosen_ms:.4f} best_ms={best['median_ms']:.4f} slowdown={slow:.3f}")
+    hits = sum(r["hit"] for r in out)
+    print(f"heuristic-vs-oracle: {hits}/{len(out)} picks within 1.1x of the fastest; "
+          f"worst slowdown {max(r['slowdown'] for r in out):.3f}x")
+    _write_csv("heuristic.csv", out)
+    return 0
+
+
+def cmd_bench(args):
+    dtype = F64 if args.dtype == "f64" else F32
+    peak, src = _peak_gbs()
+    out = []
+    for w in args.workload:
+        A, rows, gather = _measure_all(w, dtype, args.iters, args.warmup)
+        print(f"=== {WORKLOADS[w]} ({args.dtype}) m={A.m} nnz={A.nnz}; HBM peak {peak:.0f} GB/s ({src}), "
+              f"gather ceiling {gather / 1e9:.1f} G/s ===")
+        for r in rows:
+            r.update(matrix=WORKLOADS[w], precision=args.dtype, frac_hbm=r["gbs"] / peak,
+                     frac_gather=A.nnz / (r["median_ms"] * 1e-3) / gather)
+            print(f"  {r['kernel']:16s} {r['median_ms'] * 1e3:9.2f} us  {r['gflops']:8.1f} GFLOP/s "
+                  f"{r['gbs']:8.1f} GB/s  {100 * r['frac_hbm']:5.1f}% HBM  {100 * r['frac_gather']:5.1f}% gather")
+            out.append(r)
+    _write_csv("bench.csv", out)
+    return 0
+
+
+def cmd_validate(args):
+    import torch
+    bad = 0
+    for w in args.workload:
+        ctx, A, M, x, y, xh = _setup(w, F64)
+        M.spmv(x, y, kernel=CSR_SCALAR)
+        torch.cuda.synchronize()
+        ref = y.cpu().numpy().copy()
+        lens = np.diff(A.rowptr).astype(np.int64)
+        rows = np.repeat(np.arange(A.m), lens)
+        abs_sum = np.bincount(rows, weights=np.abs(A.values * xh[A.colind]), minlength=A.m)
+        nu = lens * 2.0 ** -53
+        bound = 2 * 2 * (nu / (1 - nu)) * abs_sum  # two re-associated sums vs the exact value
+        for label, k, lanes, block in VARIANTS:
+            if k == BCSR or (k == ELL and w == 3) or not _usable(M, k, block):
+                continue  # BCSR re-blocks (validated against its own CPU order in tests/)
+            y.fill_(float("nan"))
+            M.spmv(x, y, kernel=k, lanes=lanes, block=block)
+            torch.cuda.synchronize()
+            got = y.cpu().numpy()
+            ok = np.array_equal(got, ref) if k in EXACT else bool(np.all(np.abs(got - ref) <= bound))
+            bad += not ok
+            print(f"  {WORKLOADS[w]:24s} {label:16s} {'bit-exact' if k in EXACT else 'gamma_n'}: "
+                  f"{'ok' if ok else 'FAIL'}")
+    print("validate:", "ok" if bad == 0 else f"{bad} failures")
+    return 1 if bad else 0
+
+
+def cmd_profile(args):
+    import torch
+    dtype = F64 if args.dtype == "f64" else F32
+    ctx, A, M, x, y, _ = _setup(args.workload[0], dtype)
+    label = {v[0]: v for v in VARIANTS}
+    if args.profile not in label:
+        raise SystemExit(f"--profile expects one of {sorted(label)}")
+    _, k, lanes, block = label[args.profile]
+    M.prepare(k, block if k == BCSR else 0)
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        M.spmv(x, y, kernel=k, lanes=lanes, block=block)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        M.spmv(x, y, kernel=k, lanes=lanes, block=block)
+    b.record()
+    b.synchronize()
+    print(f"{args.profile} on {WORKLOADS[args.workload[0]]}: {a.elapsed_time(b) / max(1, args.steps) * 1e3:.2f} us "
+          f"per launch ({args.steps} launches after {args.warmup} warm-up)")
+    return 0
+
+
+def _write_csv(name, rows):
+    if not rows:
+        return
+    os.makedirs("results", exist_ok=True)
+    keys = list(rows[0].keys())
+    with open(os.path.join("results", name), "w", newline="") as f:
+        wr = csv.DictWriter(f, fieldnames=keys)
+        wr.writeheader()
+        wr.writerows(rows)
+    print(f"wrote results/{name}")
+
+
+def main(argv=None):
+    p = argparse.ArgumentParser(prog="python -m spmvbench_b200.driver")
+    g = p.add_mutually_exclusive_group(required=True)
+    g.add_argument("--stats", action="store_true")
+    g.add_argument("--auto", action="store_true")
+    g.add_argument("--bench", action="store_true")
+    g.add_argument("--validate", action="store_true")
+    g.add_argument("--profile", metavar="KERNEL")
+    p.add_argument("--workload", type=int, nargs="+", default=[1, 2, 3, 4])
+    p.add_argument("--dtype", choices=["f64", "f32"], default="f64")
+    p.add_argument("--iters", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--steps", type=int, default=1)
+    a = p.parse_args(argv)
+    if a.stats:
+        return cmd_stats(a)
+    if a.auto:
+        return cmd_auto(a)
+    if a.bench:
+        return cmd_bench(a)
+    if a.validate:
+        return cmd_validate(a)
+    return cmd_profile(a)
+
+
+if __name__ == "__main__":
+    sys.exit(main())
