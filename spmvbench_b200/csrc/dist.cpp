@@ -68,6 +68,15 @@ spmvb_status nccl_wait(ncclComm_t comm, double timeout_s, const char* what) {
   }
 }
 
+// A non-blocking communicator may return ncclInProgress from a collective
+// while it is still being enqueued (the first call sets up connections); the
+// next NCCL call on that communicator must wait until it reports success.
+spmvb_status nccl_enqueued(ncclComm_t comm, ncclResult_t r, const char* what) {
+  if (r == ncclSuccess) return SPMVB_OK;
+  if (r != ncclInProgress) return nccl_fail(r, what);
+  return nccl_wait(comm, 120.0, what);
+}
+
 double init_timeout_s() {
   const char* e = std::getenv("SPMVB_NCCL_INIT_TIMEOUT_S");
   return (e && *e) ? std::atof(e) : 120.0;
@@ -204,8 +213,8 @@ static spmvb_status dist_step(spmvb_dist D, spmvb_kernel kernel, int lanes, cuda
   SPMVB_TRY(spmvb_spmv(D->local, kernel, lanes, 4, D->x_pad.get(), D->y_loc.get(), D->dtype, s));
   if (D->nranks > 1) {
     const ncclDataType_t t = D->dtype == SPMVB_F64 ? ncclFloat64 : ncclFloat32;
-    ncclResult_t r = ncclAllGather(D->y_loc.get(), D->x_pad.get(), size_t(D->max_rows), t, D->comm, s);
-    if (r != ncclSuccess && r != ncclInProgress) return nccl_fail(r, "ncclAllGather");
+    SPMVB_TRY(nccl_enqueued(D->comm, ncclAllGather(D->y_loc.get(), D->x_pad.get(), size_t(D->max_rows), t, D->comm, s),
+                            "ncclAllGather"));
   } else {
     SPMVB_TRY_CUDA(cudaMemcpyAsync(D->x_pad.get(), D->y_loc.get(), size_t(D->max_rows) * dtype_size(D->dtype),
                                    cudaMemcpyDeviceToDevice, s));
@@ -235,8 +244,8 @@ spmvb_status spmvb_dist_iterate_timed(spmvb_dist D, spmvb_kernel kernel, int lan
     SPMVB_TRY_CUDA(cudaEventRecord(D->ev[1], s));
     if (D->nranks > 1) {
       const ncclDataType_t t = D->dtype == SPMVB_F64 ? ncclFloat64 : ncclFloat32;
-      ncclResult_t r = ncclAllGather(D->y_loc.get(), D->x_pad.get(), size_t(D->max_rows), t, D->comm, s);
-      if (r != ncclSuccess && r != ncclInProgress) return nccl_fail(r, "ncclAllGather");
+      SPMVB_TRY(nccl_enqueued(D->comm, ncclAllGather(D->y_loc.get(), D->x_pad.get(), size_t(D->max_rows), t, D->comm, s),
+                              "ncclAllGather"));
     } else {
       SPMVB_TRY_CUDA(cudaMemcpyAsync(D->x_pad.get(), D->y_loc.get(), size_t(D->max_rows) * dtype_size(D->dtype),
                                      cudaMemcpyDeviceToDevice, s));
