@@ -53,7 +53,10 @@ spmvb_status nccl_fail(ncclResult_t r, const char* what) {
   return fail(SPMVB_ERR_NCCL, std::string(what) + ": " + ncclGetErrorString(r));
 }
 
-// Bounded wait for a non-blocking communicator operation to settle.
+// Bounded wait for a non-blocking communicator operation to settle. A
+// collective's enqueue settles in microseconds, so the first 20 ms poll with
+// a yield between tries; only a slow operation (communicator set-up) falls
+// back to 1 ms sleeps.
 spmvb_status nccl_wait(ncclComm_t comm, double timeout_s, const char* what) {
   const auto t0 = std::chrono::steady_clock::now();
   for (;;) {
@@ -64,7 +67,10 @@ spmvb_status nccl_wait(ncclComm_t comm, double timeout_s, const char* what) {
     if (st != ncclInProgress) return nccl_fail(st, what);
     const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
     if (el > timeout_s) return fail(SPMVB_ERR_TIMEOUT, std::string(what) + ": timed out after " + std::to_string(timeout_s) + " s");
-    std::this_thread::sleep_for(std::chrono::milliseconds(1));
+    if (el < 0.02)
+      std::this_thread::yield();
+    else
+      std::this_thread::sleep_for(std::chrono::milliseconds(1));
   }
 }
 
