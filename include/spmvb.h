@@ -319,17 +319,41 @@ spmvb_status spmvb_dist_create(spmvb_context ctx, int nranks, int rank,
 spmvb_status spmvb_dist_destroy(spmvb_dist D);
 /* Load the global x (host, m entries) into this rank's padded x buffer. */
 spmvb_status spmvb_dist_set_x(spmvb_dist D, const void* h_x, void* stream);
-/* `iters` steps of: y_local = A_local x (kernel), then ncclAllGather of the
- * padded y slices into x. The final x (global, m entries) can be read back
- * with spmvb_dist_get_x. */
+/* `iters` steps of: y_local = A_local x (kernel), then the exchange of the
+ * padded y slices into x (ncclAllGather, or the peer exchange below). The
+ * final x (global, m entries) can be read back with spmvb_dist_get_x. */
 spmvb_status spmvb_dist_iterate(spmvb_dist D, spmvb_kernel kernel, int lanes,
                                 int iters, void* stream);
-/* Same, timing only the local SpMV of each step on device events; returns
- * per-step kernel milliseconds summed over the steps in *kernel_ms. */
+/* Same, with the steps enqueued back to back and timed on device events:
+ * *step_ms = milliseconds from the first step's start to the last step's
+ * end; *kernel_ms = the SpMV part of each step (for the fused peer ELL step,
+ * the whole step), summed over the steps. */
 spmvb_status spmvb_dist_iterate_timed(spmvb_dist D, spmvb_kernel kernel,
                                       int lanes, int iters, void* stream,
                                       double* kernel_ms, double* step_ms);
 spmvb_status spmvb_dist_get_x(spmvb_dist D, void* h_x, void* stream);
+
+/* Exchange of x slices between the steps of spmvb_dist_iterate. */
+typedef enum {
+  SPMVB_EXCHANGE_NCCL = 0, /* SpMV, then ncclAllGather (default) */
+  SPMVB_EXCHANGE_PEER = 1  /* SpMV stores each slice into every rank's x */
+} spmvb_exchange;
+/* Collective (every rank calls it): switch to the peer exchange. Each rank
+ * maps the other ranks' double-buffered x and phase counters through CUDA
+ * IPC; a step then runs the SpMV, stores its slice straight into every
+ * rank's next x over NVLink and ends in a barrier (its last CTA publishes
+ * this rank's phase and waits for every other rank's): one kernel for
+ * SPMVB_ELL, the SpMV plus a copy kernel for the others. With one rank the
+ * SpMV writes the next x itself. No NCCL call is on the data path.
+ * Needs one GPU per rank and at most 8 ranks; otherwise every rank gets
+ * SPMVB_ERR_UNSUPPORTED and stays on ncclAllGather. Waits give up after
+ * SPMVB_PEER_TIMEOUT_MS (environment, default 10000) with
+ * SPMVB_ERR_TIMEOUT, after which the handle only accepts destroy. Until
+ * destroy, every rank must make the same sequence of set_x / iterate /
+ * get_x calls. No reference counterpart. */
+spmvb_status spmvb_dist_enable_peer(spmvb_dist D, void* stream);
+/* SPMVB_EXCHANGE_NCCL or SPMVB_EXCHANGE_PEER. */
+int spmvb_dist_exchange(spmvb_dist D);
 spmvb_status spmvb_dist_get_info(spmvb_dist D, int32_t* row_begin,
                                  int32_t* row_end, int32_t* max_rows,
                                  int64_t* local_nnz);

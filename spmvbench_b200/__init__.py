@@ -306,7 +306,8 @@ class DeviceMatrix:
 
 class DistMatrix:
     """One rank's shard of a row-partitioned square matrix for iterated
-    y = A x, x <- y, with the x slices exchanged by ncclAllGather."""
+    y = A x, x <- y, with the x slices exchanged by ncclAllGather or, after
+    enable_peer(), stored by the SpMV into every rank's x over peer memory."""
 
     def __init__(self, ctx: Context, nranks: int, rank: int, uid: bytes | None, A: CsrMatrix,
                  bounds: np.ndarray, dtype: int = F64):
@@ -340,6 +341,16 @@ class DistMatrix:
         call("spmvb_dist_iterate_timed", self.handle, kernel, lanes, iters, _stream_ptr(stream),
              C.byref(k), C.byref(s))
         return k.value, s.value
+
+    def enable_peer(self, stream=None):
+        """Collective: switch the x exchange from ncclAllGather to direct
+        stores into every rank's x over peer memory (raises SpmvbError with
+        status UNSUPPORTED on every rank when some rank cannot map it)."""
+        call("spmvb_dist_enable_peer", self.handle, _stream_ptr(stream))
+
+    @property
+    def exchange(self) -> str:
+        return "peer" if load().spmvb_dist_exchange(self.handle) == 1 else "nccl"
 
     def get_x(self, stream=None) -> np.ndarray:
         out = np.empty(self.m, _np_dtype(self.dtype))

@@ -358,7 +358,9 @@ spmvb_status spmvb_matrix_export_bcsr(spmvb_matrix A, int block, int32_t* h_rowp
 }
 
 // Reads the context's device error word after `s` has been synchronized.
-static spmvb_status check_err_word(spmvb_context ctx, cudaStream_t s) {
+}  // extern "C"
+
+spmvb_status spmvb::check_err_word(spmvb_context ctx, cudaStream_t s) {
   int code = 0;
   SPMVB_TRY_CUDA(cudaMemcpyAsync(&code, ctx->err.get(), sizeof(int), cudaMemcpyDeviceToHost, s));
   SPMVB_TRY_CUDA(cudaStreamSynchronize(s));
@@ -368,6 +370,8 @@ static spmvb_status check_err_word(spmvb_context ctx, cudaStream_t s) {
   }
   return SPMVB_OK;
 }
+
+extern "C" {
 
 static spmvb_status check_pair(spmvb_matrix A, spmvb_dtype acc) {
   if (!A) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null matrix");

@@ -12,6 +12,16 @@
 // with no other copies. Communicator set-up is non-blocking with a bounded
 // wait: a rank that never joins makes spmvb_dist_create return
 // SPMVB_ERR_TIMEOUT after the communicator is aborted.
+//
+// Peer exchange (spmvb_dist_enable_peer, collective): every rank maps the
+// other ranks' x buffers through CUDA IPC and the step becomes
+//   y_local = A_local * x[cur]; store y_local into x[cur^1] of every rank;
+//   barrier (publish this rank's phase, wait for every peer's)
+// in one kernel for ELL (peer.cu) and SpMV + push for the other kernels,
+// with no NCCL call on the data path. x is double-buffered: step k reads
+// x[k%2] and writes x[(k+1)%2]; a rank's step k+1 writes a peer's x[k%2]
+// only after its own step k barrier, which needs the peer to have finished
+// step k, and with it every read of x[k%2].
 #include <cuda_runtime.h>
 #include <nccl.h>
 
@@ -38,11 +48,27 @@ struct spmvb_dist_st {
   int32_t max_rows = 0;
   spmvb_matrix local = nullptr;
   DevBuf x_pad, y_loc;
-  cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
 
+  // Peer exchange state.
+  bool peer = false;
+  bool broken = false;       // a peer wait gave up; the phases no longer agree
+  DevBuf pmem;               // [x0 | x1 | nranks phase counters], IPC-exported
+  size_t xbytes = 0;         // bytes of one padded x buffer (256-aligned)
+  void* peer_base[kMaxRanks] = {};  // other ranks' pmem, mapped here
+  DevBuf counter;            // finished-CTA counter of the peer kernels
+  unsigned long long phase = 0;
+  int cur = 0;
+  unsigned long long timeout_ns = 0;
+
+  void close_peers() {
+    for (int q = 0; q < kMaxRanks; ++q)
+      if (peer_base[q]) {
+        cudaIpcCloseMemHandle(peer_base[q]);
+        peer_base[q] = nullptr;
+      }
+  }
   ~spmvb_dist_st() {
-    for (auto& e : ev)
-      if (e) cudaEventDestroy(e);
+    close_peers();
     spmvb_matrix_destroy(local);
   }
 };
@@ -81,6 +107,48 @@ spmvb_status nccl_enqueued(ncclComm_t comm, ncclResult_t r, const char* what) {
   if (r == ncclSuccess) return SPMVB_OK;
   if (r != ncclInProgress) return nccl_fail(r, what);
   return nccl_wait(comm, 120.0, what);
+}
+
+double peer_timeout_ms() {
+  const char* e = std::getenv("SPMVB_PEER_TIMEOUT_MS");
+  const double v = (e && *e) ? std::atof(e) : 10000.0;
+  return v > 0 ? v : 10000.0;
+}
+
+unsigned char* x_buf(spmvb_dist D, int which) { return D->pmem.as<unsigned char>() + size_t(which) * D->xbytes; }
+
+// Kernel view of the next peer operation: write this rank's slice of
+// x[cur^1] of every rank, then publish phase D->phase + 1 and wait for every
+// peer to reach it.
+PeerView peer_view(spmvb_dist D) {
+  PeerView P;
+  const size_t es = dtype_size(D->dtype);
+  const size_t slice = size_t(D->rank) * D->max_rows * es;
+  const size_t next = size_t(D->cur ^ 1) * D->xbytes + slice;
+  const size_t flags = 2 * D->xbytes;
+  for (int q = 0; q < D->nranks; ++q) {
+    unsigned char* base = q == D->rank ? D->pmem.as<unsigned char>() : static_cast<unsigned char*>(D->peer_base[q]);
+    P.dst[q] = base + next;
+    P.flag_out[q] = reinterpret_cast<unsigned long long*>(base + flags) + D->rank;
+  }
+  P.flags_in = reinterpret_cast<const unsigned long long*>(D->pmem.as<unsigned char>() + flags);
+  P.counter = D->counter.as<unsigned int>();
+  P.err = D->ctx->err.as<int>();
+  P.publish = D->phase + 1;
+  P.timeout_ns = D->timeout_ns;
+  P.nranks = D->nranks;
+  P.rank = D->rank;
+  P.rows = D->bounds[D->rank + 1] - D->bounds[D->rank];
+  return P;
+}
+
+// Reads the device error word after a peer operation; a peer wait that gave
+// up leaves the ranks' phases out of step, so the handle refuses further
+// steps.
+spmvb_status peer_check(spmvb_dist D, cudaStream_t s) {
+  const spmvb_status st = check_err_word(D->ctx, s);
+  if (st == SPMVB_ERR_TIMEOUT) D->broken = true;
+  return st;
 }
 
 double init_timeout_s() {
@@ -165,7 +233,6 @@ spmvb_status spmvb_dist_create(spmvb_context ctx, int nranks, int rank, const vo
   SPMVB_TRY(spmvb_matrix_create_csr(ctx, dtype, ml, npad, lnnz, rp.data(), ci.data(), vv, &D->local));
   SPMVB_TRY(D->x_pad.alloc(size_t(std::max(npad, 1)) * es));
   SPMVB_TRY(D->y_loc.alloc(size_t(std::max(D->max_rows, 1)) * es));
-  for (auto& e : D->ev) SPMVB_TRY_CUDA(cudaEventCreate(&e));
 
   if (nranks > 1) {
     ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
@@ -190,6 +257,17 @@ spmvb_status spmvb_dist_destroy(spmvb_dist D) {
   clear_error();
   if (!D) return SPMVB_OK;
   DeviceGuard g(D->ctx->device);
+  if (D->peer && D->nranks > 1) {
+    // A last barrier: once every rank has reached it, no rank stores into
+    // another's buffers again. If it fails, the buffers are left allocated
+    // rather than freed under a possible writer.
+    bool quiet = cudaDeviceSynchronize() == cudaSuccess && !D->broken;
+    if (quiet) {
+      quiet = peer_launch_barrier(peer_view(D), nullptr) == SPMVB_OK && check_err_word(D->ctx, nullptr) == SPMVB_OK;
+    }
+    D->close_peers();
+    if (!quiet) (void)D->pmem.release();
+  }
   if (D->comm) {
     ncclCommFinalize(D->comm);
     nccl_wait(D->comm, 30.0, "ncclCommFinalize");
@@ -199,9 +277,98 @@ spmvb_status spmvb_dist_destroy(spmvb_dist D) {
   return SPMVB_OK;
 }
 
+spmvb_status spmvb_dist_enable_peer(spmvb_dist D, void* stream) {
+  clear_error();
+  if (!D) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null argument");
+  if (D->peer) return SPMVB_OK;
+  if (D->nranks > kMaxRanks)
+    return fail(SPMVB_ERR_UNSUPPORTED, "the peer exchange supports at most " + std::to_string(kMaxRanks) + " ranks");
+  DeviceGuard g(D->ctx->device);
+  auto s = static_cast<cudaStream_t>(stream);
+  const size_t es = dtype_size(D->dtype);
+  const size_t npad_bytes = size_t(D->nranks) * D->max_rows * es;
+  D->xbytes = std::max<size_t>(256, (npad_bytes + 255) / 256 * 256);
+  SPMVB_TRY(D->pmem.alloc(2 * D->xbytes + 256));
+  SPMVB_TRY(D->counter.alloc(256));
+  D->timeout_ns = static_cast<unsigned long long>(peer_timeout_ms() * 1e6);
+  // The zero-filled counters must be in place before any rank can map them.
+  SPMVB_TRY_CUDA(cudaDeviceSynchronize());
+
+  if (D->nranks > 1) {
+    struct Record {
+      cudaIpcMemHandle_t handle;
+      unsigned char uuid[16];
+      int32_t ok;
+      int32_t pad[3];
+    };
+    Record mine;
+    std::memset(&mine, 0, sizeof(mine));
+    mine.ok = cudaIpcGetMemHandle(&mine.handle, D->pmem.get()) == cudaSuccess;
+    cudaGetLastError();
+    cudaDeviceProp prop;
+    SPMVB_TRY_CUDA(cudaGetDeviceProperties(&prop, D->ctx->device));
+    std::memcpy(mine.uuid, &prop.uuid, sizeof(mine.uuid));
+    std::vector<Record> all(D->nranks);
+    DevBuf dsend, drecv, dok;
+    SPMVB_TRY(dsend.alloc(sizeof(Record)));
+    SPMVB_TRY(drecv.alloc(sizeof(Record) * D->nranks));
+    SPMVB_TRY(dok.alloc(sizeof(int32_t)));
+    SPMVB_TRY_CUDA(cudaMemcpyAsync(dsend.get(), &mine, sizeof(Record), cudaMemcpyHostToDevice, s));
+    SPMVB_TRY(nccl_enqueued(D->comm, ncclAllGather(dsend.get(), drecv.get(), sizeof(Record), ncclChar, D->comm, s),
+                            "ncclAllGather(peer records)"));
+    SPMVB_TRY_CUDA(cudaMemcpyAsync(all.data(), drecv.get(), sizeof(Record) * D->nranks, cudaMemcpyDeviceToHost, s));
+    SPMVB_TRY_CUDA(cudaStreamSynchronize(s));
+
+    // Every rank sees the same records, so these checks agree everywhere.
+    std::string why;
+    for (int q = 0; q < D->nranks && why.empty(); ++q)
+      if (!all[q].ok) why = "rank " + std::to_string(q) + " could not export its buffers";
+    for (int q = 0; q < D->nranks && why.empty(); ++q)
+      for (int r = q + 1; r < D->nranks && why.empty(); ++r)
+        if (std::memcmp(all[q].uuid, all[r].uuid, sizeof(all[q].uuid)) == 0)
+          why = "ranks " + std::to_string(q) + " and " + std::to_string(r) +
+                " share one GPU; the peer kernels wait on one another and need one GPU per rank";
+    int32_t ok = why.empty();
+    for (int q = 0; q < D->nranks && ok; ++q) {
+      if (q == D->rank) continue;
+      const cudaError_t e = cudaIpcOpenMemHandle(&D->peer_base[q], all[q].handle, cudaIpcMemLazyEnablePeerAccess);
+      if (e != cudaSuccess) {
+        cudaGetLastError();
+        D->peer_base[q] = nullptr;
+        ok = 0;
+        why = "cudaIpcOpenMemHandle(rank " + std::to_string(q) + "): " + cudaGetErrorString(e);
+      }
+    }
+    // All ranks must agree before any of them stores into another's memory.
+    SPMVB_TRY_CUDA(cudaMemcpyAsync(dok.get(), &ok, sizeof(ok), cudaMemcpyHostToDevice, s));
+    SPMVB_TRY(nccl_enqueued(D->comm, ncclAllReduce(dok.get(), dok.get(), 1, ncclInt32, ncclMin, D->comm, s),
+                            "ncclAllReduce(peer agreement)"));
+    int32_t all_ok = 0;
+    SPMVB_TRY_CUDA(cudaMemcpyAsync(&all_ok, dok.get(), sizeof(all_ok), cudaMemcpyDeviceToHost, s));
+    SPMVB_TRY_CUDA(cudaStreamSynchronize(s));
+    if (!all_ok) {
+      D->close_peers();
+      D->pmem.reset();
+      D->counter.reset();
+      return fail(SPMVB_ERR_UNSUPPORTED,
+                  "peer exchange unavailable: " + (why.empty() ? std::string("another rank could not map peer memory") : why));
+    }
+  }
+  if (npad_bytes)
+    SPMVB_TRY_CUDA(cudaMemcpyAsync(x_buf(D, 0), D->x_pad.get(), npad_bytes, cudaMemcpyDeviceToDevice, s));
+  SPMVB_TRY_CUDA(cudaStreamSynchronize(s));
+  D->cur = 0;
+  D->phase = 0;
+  D->peer = true;
+  return SPMVB_OK;
+}
+
+int spmvb_dist_exchange(spmvb_dist D) { return D && D->peer ? SPMVB_EXCHANGE_PEER : SPMVB_EXCHANGE_NCCL; }
+
 spmvb_status spmvb_dist_set_x(spmvb_dist D, const void* h_x, void* stream) {
   clear_error();
   if (!D || (D->m && !h_x)) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null argument");
+  if (D->broken) return fail(SPMVB_ERR_TIMEOUT, "an earlier peer wait gave up; recreate the handle");
   DeviceGuard g(D->ctx->device);
   const size_t es = dtype_size(D->dtype);
   std::vector<unsigned char> pad(size_t(D->nranks) * D->max_rows * es, 0);
@@ -210,8 +377,36 @@ spmvb_status spmvb_dist_set_x(spmvb_dist D, const void* h_x, void* stream) {
     std::memcpy(pad.data() + size_t(r) * D->max_rows * es, static_cast<const unsigned char*>(h_x) + size_t(b) * es, size_t(cnt) * es);
   }
   auto s = static_cast<cudaStream_t>(stream);
-  if (!pad.empty()) SPMVB_TRY_CUDA(cudaMemcpyAsync(D->x_pad.get(), pad.data(), pad.size(), cudaMemcpyHostToDevice, s));
+  if (!D->peer) {
+    if (!pad.empty()) SPMVB_TRY_CUDA(cudaMemcpyAsync(D->x_pad.get(), pad.data(), pad.size(), cudaMemcpyHostToDevice, s));
+    SPMVB_TRY_CUDA(cudaStreamSynchronize(s));
+    return SPMVB_OK;
+  }
+  // Peer exchange: the previous operation's barrier saw every peer's stores
+  // into x[cur] land, and no peer writes x[cur] before this rank's next step
+  // has read it.
+  if (!pad.empty()) SPMVB_TRY_CUDA(cudaMemcpyAsync(x_buf(D, D->cur), pad.data(), pad.size(), cudaMemcpyHostToDevice, s));
   SPMVB_TRY_CUDA(cudaStreamSynchronize(s));
+  return SPMVB_OK;
+}
+
+// One peer-exchange step. One rank: the SpMV writes the other x buffer.
+// Several: the fused ELL kernel, or the SpMV into y_loc and the push kernel.
+static spmvb_status peer_step(spmvb_dist D, spmvb_kernel kernel, int lanes, cudaStream_t s, cudaEvent_t mark) {
+  void* x = x_buf(D, D->cur);
+  if (D->nranks == 1) {
+    SPMVB_TRY(spmvb_spmv(D->local, kernel, lanes, 4, x, x_buf(D, D->cur ^ 1), D->dtype, s));
+    if (mark) SPMVB_TRY_CUDA(cudaEventRecord(mark, s));
+  } else if (kernel == SPMVB_ELL) {
+    SPMVB_TRY(peer_launch_ell(D->local, peer_view(D), x, s));
+    if (mark) SPMVB_TRY_CUDA(cudaEventRecord(mark, s));
+  } else {
+    SPMVB_TRY(spmvb_spmv(D->local, kernel, lanes, 4, x, D->y_loc.get(), D->dtype, s));
+    if (mark) SPMVB_TRY_CUDA(cudaEventRecord(mark, s));
+    SPMVB_TRY(peer_launch_push(D->dtype, D->y_loc.get(), peer_view(D), D->ctx->sm_count, s));
+  }
+  D->cur ^= 1;
+  D->phase += 1;
   return SPMVB_OK;
 }
 
@@ -231,8 +426,13 @@ static spmvb_status dist_step(spmvb_dist D, spmvb_kernel kernel, int lanes, cuda
 spmvb_status spmvb_dist_iterate(spmvb_dist D, spmvb_kernel kernel, int lanes, int iters, void* stream) {
   clear_error();
   if (!D || iters < 0) return fail(SPMVB_ERR_INVALID_ARGUMENT, "bad argument");
+  if (D->broken) return fail(SPMVB_ERR_TIMEOUT, "an earlier peer wait gave up; recreate the handle");
   DeviceGuard g(D->ctx->device);
   auto s = static_cast<cudaStream_t>(stream);
+  if (D->peer) {
+    for (int it = 0; it < iters; ++it) SPMVB_TRY(peer_step(D, kernel, lanes, s, nullptr));
+    return peer_check(D, s);
+  }
   for (int it = 0; it < iters; ++it) SPMVB_TRY(dist_step(D, kernel, lanes, s));
   return SPMVB_OK;
 }
@@ -241,42 +441,67 @@ spmvb_status spmvb_dist_iterate_timed(spmvb_dist D, spmvb_kernel kernel, int lan
                                       double* kernel_ms, double* step_ms) {
   clear_error();
   if (!D || iters < 0 || !kernel_ms || !step_ms) return fail(SPMVB_ERR_INVALID_ARGUMENT, "bad argument");
+  if (D->broken) return fail(SPMVB_ERR_TIMEOUT, "an earlier peer wait gave up; recreate the handle");
   DeviceGuard g(D->ctx->device);
   auto s = static_cast<cudaStream_t>(stream);
-  double k_ms = 0.0, st_ms = 0.0;
-  for (int it = 0; it < iters; ++it) {
-    SPMVB_TRY_CUDA(cudaEventRecord(D->ev[0], s));
-    SPMVB_TRY(spmvb_spmv(D->local, kernel, lanes, 4, D->x_pad.get(), D->y_loc.get(), D->dtype, s));
-    SPMVB_TRY_CUDA(cudaEventRecord(D->ev[1], s));
-    if (D->nranks > 1) {
-      const ncclDataType_t t = D->dtype == SPMVB_F64 ? ncclFloat64 : ncclFloat32;
-      SPMVB_TRY(nccl_enqueued(D->comm, ncclAllGather(D->y_loc.get(), D->x_pad.get(), size_t(D->max_rows), t, D->comm, s),
-                              "ncclAllGather"));
-    } else {
-      SPMVB_TRY_CUDA(cudaMemcpyAsync(D->x_pad.get(), D->y_loc.get(), size_t(D->max_rows) * dtype_size(D->dtype),
-                                     cudaMemcpyDeviceToDevice, s));
+  *kernel_ms = 0.0;
+  *step_ms = 0.0;
+  if (iters == 0) return SPMVB_OK;
+  // Steps are enqueued back to back (no host synchronization between them);
+  // event i*2 opens step i, i*2+1 follows its SpMV, the last closes the run.
+  struct Events {
+    std::vector<cudaEvent_t> e;
+    ~Events() {
+      for (auto v : e)
+        if (v) cudaEventDestroy(v);
     }
-    SPMVB_TRY_CUDA(cudaEventRecord(D->ev[2], s));
-    SPMVB_TRY_CUDA(cudaEventSynchronize(D->ev[2]));
-    float a = 0.f, b = 0.f;
-    SPMVB_TRY_CUDA(cudaEventElapsedTime(&a, D->ev[0], D->ev[1]));
-    SPMVB_TRY_CUDA(cudaEventElapsedTime(&b, D->ev[0], D->ev[2]));
-    k_ms += a;
-    st_ms += b;
+  } ev;
+  ev.e.resize(size_t(2) * iters + 1, nullptr);
+  for (auto& v : ev.e) SPMVB_TRY_CUDA(cudaEventCreate(&v));
+  for (int it = 0; it < iters; ++it) {
+    SPMVB_TRY_CUDA(cudaEventRecord(ev.e[2 * it], s));
+    if (D->peer) {
+      SPMVB_TRY(peer_step(D, kernel, lanes, s, ev.e[2 * it + 1]));
+    } else {
+      SPMVB_TRY(spmvb_spmv(D->local, kernel, lanes, 4, D->x_pad.get(), D->y_loc.get(), D->dtype, s));
+      SPMVB_TRY_CUDA(cudaEventRecord(ev.e[2 * it + 1], s));
+      if (D->nranks > 1) {
+        const ncclDataType_t t = D->dtype == SPMVB_F64 ? ncclFloat64 : ncclFloat32;
+        SPMVB_TRY(nccl_enqueued(D->comm, ncclAllGather(D->y_loc.get(), D->x_pad.get(), size_t(D->max_rows), t, D->comm, s),
+                                "ncclAllGather"));
+      } else {
+        SPMVB_TRY_CUDA(cudaMemcpyAsync(D->x_pad.get(), D->y_loc.get(), size_t(D->max_rows) * dtype_size(D->dtype),
+                                       cudaMemcpyDeviceToDevice, s));
+      }
+    }
   }
+  SPMVB_TRY_CUDA(cudaEventRecord(ev.e[2 * iters], s));
+  SPMVB_TRY_CUDA(cudaEventSynchronize(ev.e[2 * iters]));
+  if (D->peer) SPMVB_TRY(peer_check(D, s));
+  double k_ms = 0.0;
+  for (int it = 0; it < iters; ++it) {
+    float a = 0.f;
+    SPMVB_TRY_CUDA(cudaEventElapsedTime(&a, ev.e[2 * it], ev.e[2 * it + 1]));
+    k_ms += a;
+  }
+  float b = 0.f;
+  SPMVB_TRY_CUDA(cudaEventElapsedTime(&b, ev.e[0], ev.e[2 * iters]));
   *kernel_ms = k_ms;
-  *step_ms = st_ms;
+  *step_ms = b;
   return SPMVB_OK;
 }
 
 spmvb_status spmvb_dist_get_x(spmvb_dist D, void* h_x, void* stream) {
   clear_error();
   if (!D || (D->m && !h_x)) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null argument");
+  if (D->broken) return fail(SPMVB_ERR_TIMEOUT, "an earlier peer wait gave up; recreate the handle");
   DeviceGuard g(D->ctx->device);
   const size_t es = dtype_size(D->dtype);
   std::vector<unsigned char> pad(size_t(D->nranks) * D->max_rows * es);
   auto s = static_cast<cudaStream_t>(stream);
-  if (!pad.empty()) SPMVB_TRY_CUDA(cudaMemcpyAsync(pad.data(), D->x_pad.get(), pad.size(), cudaMemcpyDeviceToHost, s));
+  // Peer exchange: the last step's barrier saw every peer's stores land.
+  const void* src = D->peer ? x_buf(D, D->cur) : D->x_pad.get();
+  if (!pad.empty()) SPMVB_TRY_CUDA(cudaMemcpyAsync(pad.data(), src, pad.size(), cudaMemcpyDeviceToHost, s));
   SPMVB_TRY_CUDA(cudaStreamSynchronize(s));
   for (int r = 0; r < D->nranks; ++r) {
     const int32_t b = D->bounds[r], cnt = D->bounds[r + 1] - b;

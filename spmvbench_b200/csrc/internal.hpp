@@ -74,6 +74,13 @@ class DevBuf {
   void* get() const { return p_; }
   template <typename U> U* as() const { return static_cast<U*>(p_); }
   size_t bytes() const { return bytes_; }
+  // Gives up ownership without freeing (the allocation outlives the handle).
+  void* release() {
+    void* p = p_;
+    p_ = nullptr;
+    bytes_ = 0;
+    return p;
+  }
 
  private:
   void* p_ = nullptr;
@@ -194,5 +201,14 @@ template <typename T, typename Acc>
 spmvb_status launch_spmm(spmvb_matrix A, int tile, int bucketed, int k,
                          const T* X, Acc* Y, cudaStream_t stream);
 spmvb_status launch_merge_partition(spmvb_matrix A, cudaStream_t stream);
+
+// Reads (stream-ordered, then synchronizes) and clears the context's device
+// error word; SPMVB_ERR_TIMEOUT if a kernel's bounded wait gave up.
+spmvb_status check_err_word(spmvb_context ctx, cudaStream_t s);
+
+// Peer-memory exchange launchers (peer.cu).
+spmvb_status peer_launch_ell(spmvb_matrix A, const PeerView& P, const void* x, cudaStream_t s);
+spmvb_status peer_launch_push(spmvb_dtype dtype, const void* y, const PeerView& P, int sm_count, cudaStream_t s);
+spmvb_status peer_launch_barrier(const PeerView& P, cudaStream_t s);
 
 }  // namespace spmvb

@@ -1,0 +1,171 @@
+// Kernels of the peer-memory exchange for row-sharded iterated SpMV (no
+// reference counterpart; the reference is single-GPU).
+//
+// Each rank maps every other rank's x buffers and phase counters (CUDA IPC,
+// set up by spmvb_dist_enable_peer) and, instead of a separate all-gather,
+// stores its slice of the next x straight into every rank's buffer over
+// NVLink while it computes it.
+//
+// Every peer operation ends in a barrier run by the last CTA of its final
+// kernel: CTAs count themselves finished with a gpu-scope release (their
+// stores, local and remote, ordered before it); the last one fences at
+// system scope, writes the new phase number into every other rank's counter
+// for this rank, then waits until every other rank's counter for it reaches
+// the same phase. The next kernel on the stream starts after that, so it
+// reads x with no wait of its own, and a rank stores into a peer's x buffer
+// only after that peer has finished the step that read it.
+//
+//   ell_rows_peer  one launch per step: ELL rows (same order as ell_rows, so
+//                  bit-identical to csr_omp), each row's sum stored to every
+//                  rank, barrier.
+//   peer_push      after a non-fused SpMV: copy the local slice to every
+//                  rank, barrier.
+//   peer_barrier   barrier only.
+//
+// The wait is bounded by a wall-clock limit (%globaltimer) and an iteration
+// cap; a wait that gives up writes kErrPeerWait to the context error word.
+// Once the word is set no barrier publishes or waits, so every later step
+// and every other rank gives up too instead of reading stale x.
+#include <algorithm>
+#include <cstdint>
+
+#include "internal.hpp"
+#include "spmv_kernels.cuh"
+
+namespace spmvb {
+
+namespace {
+
+constexpr int kErrPeerWait = 3;
+constexpr int kPeerRowThreads = 256;
+constexpr uint32_t kPeerSpinCap = 1u << 28;
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ int ld_volatile(const int* p) { return *static_cast<const volatile int*>(p); }
+
+// One thread: true once every other rank's counter for this rank has
+// reached `phase`, false if the error word is (or becomes) set or the wait
+// runs past P.timeout_ns.
+__device__ bool peer_wait_all(const PeerView& P, unsigned long long phase) {
+  const unsigned long long t0 = globaltimer_ns();
+  for (int q = 0; q < P.nranks; ++q) {
+    if (q == P.rank) continue;
+    uint32_t spins = 0;
+    while (ld_acquire_sys(P.flags_in + q) < phase) {
+      ++spins;
+      if ((spins & 63) == 0) {
+        if (ld_volatile(P.err) != 0) return false;
+        if (globaltimer_ns() - t0 > P.timeout_ns || spins >= kPeerSpinCap) {
+          atomicExch(P.err, kErrPeerWait);
+          return false;
+        }
+      }
+      __nanosleep(64);
+    }
+  }
+  return true;
+}
+
+// All threads of every CTA, after the CTA's last store: the barrier above.
+__device__ void peer_arrive(const PeerView& P) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(P.counter) : "memory");
+    if (prev == gridDim.x - 1) {
+      __threadfence_system();
+      atomicExch(P.counter, 0u);
+      if (ld_volatile(P.err) == 0) {
+#pragma unroll
+        for (int q = 0; q < kMaxRanks; ++q)
+          if (q < P.nranks && q != P.rank) st_release_sys(P.flag_out[q], P.publish);
+        peer_wait_all(P, P.publish);
+      }
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void store_all(const PeerView& P, int i, T v) {
+#pragma unroll
+  for (int q = 0; q < kMaxRanks; ++q)
+    if (q < P.nranks) static_cast<T*>(P.dst[q])[i] = v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kPeerRowThreads) ell_rows_peer(EllView E, const T* __restrict__ x, PeerView P) {
+  const uint64_t ps = policy_evict_first();
+  const uint64_t pk = policy_evict_last();
+  for (int row = blockIdx.x * blockDim.x + threadIdx.x; row < E.m; row += gridDim.x * blockDim.x)
+    store_all<T>(P, row, ell_row_sum<T, T>(E, row, E.row_lengths[row], x, ps, pk));
+  peer_arrive(P);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) peer_push(const T* __restrict__ y, PeerView P) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < P.rows; i += gridDim.x * blockDim.x)
+    store_all<T>(P, i, y[i]);
+  peer_arrive(P);
+}
+
+__global__ void peer_barrier(PeerView P) { peer_arrive(P); }
+
+}  // namespace
+
+// Grid of the grid-stride peer kernels: at most 8 CTAs of 256 threads per
+// SM, so few CTAs pay for the barrier's per-CTA release.
+static int peer_grid(int rows, int sm_count) {
+  return std::max(1, std::min((rows + 255) / 256, sm_count * 8));
+}
+
+spmvb_status peer_launch_ell(spmvb_matrix A, const PeerView& P, const void* x, cudaStream_t s) {
+  SPMVB_TRY(build_ell(A));
+  EllView e;
+  e.colind = A->ell_colind.as<int>();
+  e.values = A->ell_values.get();
+  e.row_lengths = A->ell_rowlen.as<int>();
+  e.m = A->m;
+  e.n = A->n;
+  e.width = A->ell_width;
+  e.ld = A->m;
+  const int grid = peer_grid(A->m, A->ctx->sm_count);
+  if (A->dtype == SPMVB_F64)
+    ell_rows_peer<double><<<grid, kPeerRowThreads, 0, s>>>(e, static_cast<const double*>(x), P);
+  else
+    ell_rows_peer<float><<<grid, kPeerRowThreads, 0, s>>>(e, static_cast<const float*>(x), P);
+  count_launch();
+  SPMVB_TRY_CUDA(cudaGetLastError());
+  return SPMVB_OK;
+}
+
+spmvb_status peer_launch_push(spmvb_dtype dtype, const void* y, const PeerView& P, int sm_count, cudaStream_t s) {
+  const int grid = peer_grid(P.rows, sm_count);
+  if (dtype == SPMVB_F64)
+    peer_push<double><<<grid, 256, 0, s>>>(static_cast<const double*>(y), P);
+  else
+    peer_push<float><<<grid, 256, 0, s>>>(static_cast<const float*>(y), P);
+  count_launch();
+  SPMVB_TRY_CUDA(cudaGetLastError());
+  return SPMVB_OK;
+}
+
+spmvb_status peer_launch_barrier(const PeerView& P, cudaStream_t s) {
+  peer_barrier<<<1, 32, 0, s>>>(P);
+  count_launch();
+  SPMVB_TRY_CUDA(cudaGetLastError());
+  return SPMVB_OK;
+}
+
+}  // namespace spmvb

@@ -612,16 +612,11 @@ __global__ void merge_partition(CsrView A, int64_t num_items, int tile_items,
 // order. SKIP_LONG: rows with row_lengths < 0 belong to the hybrid format's
 // long-row kernel and are not written here.
 // ---------------------------------------------------------------------------
-template <typename T, typename Acc, bool SKIP_LONG>
-__global__ void __launch_bounds__(256)
-    ell_rows(EllView E, const T* __restrict__ x, Acc* __restrict__ y) {
-  const int row = blockIdx.x * blockDim.x + threadIdx.x;
-  if (row >= E.m) return;
+// Sum of ELL row `row` (L real entries), left to right from zero.
+template <typename T, typename Acc>
+__device__ __forceinline__ Acc ell_row_sum(const EllView& E, int row, int L, const T* __restrict__ x,
+                                           uint64_t ps, uint64_t pk) {
   const T* __restrict__ vals = static_cast<const T*>(E.values);
-  const uint64_t ps = policy_evict_first();
-  const uint64_t pk = policy_evict_last();
-  const int L = E.row_lengths[row];
-  if (SKIP_LONG && L < 0) return;
   Acc sum = Acc(0);
   int64_t p = row;
   int j = 0;
@@ -643,7 +638,17 @@ __global__ void __launch_bounds__(256)
                                 ld_keep(x + ld_stream(E.colind + p, ps), pk)));
     p += E.ld;
   }
-  y[row] = sum;
+  return sum;
+}
+
+template <typename T, typename Acc, bool SKIP_LONG>
+__global__ void __launch_bounds__(256)
+    ell_rows(EllView E, const T* __restrict__ x, Acc* __restrict__ y) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= E.m) return;
+  const int L = E.row_lengths[row];
+  if (SKIP_LONG && L < 0) return;
+  y[row] = ell_row_sum<T, Acc>(E, row, L, x, policy_evict_first(), policy_evict_last());
 }
 
 // Hybrid long rows: one warp per row over its K ELL slots and its CSR tail.

@@ -84,4 +84,27 @@ struct BucketView {
   int n_long = 0;
 };
 
+// Peer-memory exchange of one step of row-sharded iterated SpMV (at most
+// kMaxRanks ranks, one GPU each). Rank `rank` writes its `rows` results into
+// every rank's next x buffer (dst[p] already points at this rank's slice of
+// rank p's buffer; dst[rank] is its own). Phase counters: flags_in[q] is the
+// number of operations rank q has finished, written by rank q through
+// flag_out[...] of its own view. The operation's last CTA writes `publish`
+// to every other rank's counter for this rank once all of the operation's
+// stores are visible, then waits until all of this rank's counters reach it.
+constexpr int kMaxRanks = 8;
+
+struct PeerView {
+  void* dst[kMaxRanks] = {};
+  unsigned long long* flag_out[kMaxRanks] = {};  // &rank p's flags_in[this rank]
+  const unsigned long long* flags_in = nullptr;  // nranks counters
+  unsigned int* counter = nullptr;               // finished CTAs; 0 between launches
+  int* err = nullptr;                            // context error word
+  unsigned long long publish = 0;
+  unsigned long long timeout_ns = 0;
+  int nranks = 1;
+  int rank = 0;
+  int rows = 0;
+};
+
 }  // namespace spmvb

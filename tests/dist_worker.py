@@ -1,7 +1,8 @@
 """One rank of the multi-GPU parity test (launched by tests/test_gpu_dist.py
 under torch.distributed.run): iterated y = A x, x <- y, row-sharded over the
-ranks with ncclAllGather of the padded slices, checked bit for bit against
-the single-process oracle iteration (row sharding keeps every row's order)."""
+ranks, x slices exchanged by ncclAllGather and by the peer-memory exchange,
+checked bit for bit against the single-process oracle iteration (row
+sharding keeps every row's order; merge-path rows within 1e-9)."""
 import datetime
 import os
 import sys
@@ -23,23 +24,30 @@ for which, rows, kernel in ((2, 200000, S.ELL), (3, 300000, S.CSR_MERGE), (1, 0,
     A = S.generate(which, seed=91, scale_rows=rows)
     x0 = S.generate_vector(92, A.n) / 4.0
     bounds = S.partition_rows(A.rowptr, world)
-    obj = [S.nccl_unique_id() if rank == 0 else None]
-    dist.broadcast_object_list(obj, src=0)
-    D = S.DistMatrix(ctx, world, rank, obj[0], A, bounds, S.F64)
-    D.set_x(x0)
-    D.iterate(3, kernel=kernel)
-    got = D.get_x()
-    D.close()
     x = x0
     for _ in range(3):
         x = oracle.spmv_csr(A.m, A.rowptr, A.colind, A.values, x, np.float64)
-    if kernel == S.CSR_MERGE:
-        r, _ = oracle.gamma_ratio(A.rowptr, A.colind, A.values, x0, x, x, np.float64)
-        ok = np.allclose(got, x, rtol=1e-9, atol=0)
-    else:
-        ok = np.array_equal(got, x)
-    print(f"rank {rank} workload {which} kernel {S.kernel_name(kernel)}: {'ok' if ok else 'MISMATCH'}", flush=True)
-    bad += not ok
+    for exchange in ("nccl", "peer"):
+        obj = [S.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        D = S.DistMatrix(ctx, world, rank, obj[0], A, bounds, S.F64)
+        if exchange == "peer":
+            D.enable_peer()
+            assert D.exchange == "peer"
+            D.set_x(x0 * 3.0)   # overwritten below: set_x must wait for no one and restart cleanly
+            D.iterate(1, kernel=kernel)
+        D.set_x(x0)
+        D.iterate(2, kernel=kernel)
+        D.iterate(1, kernel=kernel)
+        got = D.get_x()
+        D.close()
+        if kernel == S.CSR_MERGE:
+            ok = np.allclose(got, x, rtol=1e-9, atol=1e-12)
+        else:
+            ok = np.array_equal(got, x)
+        print(f"rank {rank} workload {which} kernel {S.kernel_name(kernel)} exchange {exchange}: "
+              f"{'ok' if ok else 'MISMATCH'}", flush=True)
+        bad += not ok
 dist.barrier()
 dist.destroy_process_group()
 sys.exit(1 if bad else 0)

@@ -107,6 +107,34 @@ def test_single_rank_iteration_matches_oracle(ctx):
     D.close()
 
 
+@pytest.mark.parametrize("kernel", ["ELL", "CSR_MERGE", "CSR_SCALAR"])
+def test_single_rank_peer_exchange(ctx, kernel):
+    """Peer exchange with one rank: the SpMV writes the next x itself (fused
+    for ELL, SpMV + copy kernel otherwise); set_x between iterations restarts
+    from a new x. Thread-per-row kernels stay bit-identical to csr_omp."""
+    k = getattr(S, kernel)
+    A = S.generate(2, seed=78, scale_rows=60000)
+    D = S.DistMatrix(ctx, 1, 0, None, A, S.partition_rows(A.rowptr, 1), S.F64)
+    D.enable_peer()
+    assert D.exchange == "peer"
+    for seed, iters in ((79, 3), (80, 2)):
+        x0 = S.generate_vector(seed, A.n)
+        D.set_x(x0)
+        D.iterate(iters, kernel=k)
+        got = D.get_x()
+        x = x0
+        for _ in range(iters):
+            x = oracle_y(A, x, S.F64, S.F64)
+        if k == S.CSR_MERGE:
+            np.testing.assert_allclose(got, x, rtol=1e-9, atol=1e-12)
+        else:
+            assert_bitwise(x, got, f"peer {kernel}")
+    kms, sms = D.iterate_timed(2, kernel=k)
+    assert 0 < kms <= sms
+    ctx.check()
+    D.close()
+
+
 def test_bounded_wait_reports_timeout(ctx):
     """Failure detection on the GPU: a wait that nothing will satisfy gives up
     after its limit, the kernel records it, and the host gets
