@@ -55,10 +55,18 @@ struct spmvb_dist_st {
   DevBuf pmem;               // [x0 | x1 | nranks phase counters], IPC-exported
   size_t xbytes = 0;         // bytes of one padded x buffer (256-aligned)
   void* peer_base[kMaxRanks] = {};  // other ranks' pmem, mapped here
-  DevBuf counter;            // finished-CTA counter of the peer kernels
-  unsigned long long phase = 0;
+  DevBuf counter;            // finished-CTA counter (offset 0) and phase (offset 64)
   int cur = 0;
   unsigned long long timeout_ns = 0;
+  // Captured pairs of peer steps (x parity returns to where it started),
+  // keyed by kernel, lanes and starting parity.
+  struct Graph {
+    int kernel, lanes, parity;
+    cudaGraphExec_t exec;
+    uint64_t kernels;  // kernel launches per replay
+  };
+  std::vector<Graph> graphs;
+  cudaStream_t capture = nullptr;
 
   void close_peers() {
     for (int q = 0; q < kMaxRanks; ++q)
@@ -68,6 +76,8 @@ struct spmvb_dist_st {
       }
   }
   ~spmvb_dist_st() {
+    for (auto& g : graphs) cudaGraphExecDestroy(g.exec);
+    if (capture) cudaStreamDestroy(capture);
     close_peers();
     spmvb_matrix_destroy(local);
   }
@@ -118,7 +128,7 @@ double peer_timeout_ms() {
 unsigned char* x_buf(spmvb_dist D, int which) { return D->pmem.as<unsigned char>() + size_t(which) * D->xbytes; }
 
 // Kernel view of the next peer operation: write this rank's slice of
-// x[cur^1] of every rank, then publish phase D->phase + 1 and wait for every
+// x[cur^1] of every rank, then publish the next phase and wait for every
 // peer to reach it.
 PeerView peer_view(spmvb_dist D) {
   PeerView P;
@@ -134,7 +144,7 @@ PeerView peer_view(spmvb_dist D) {
   P.flags_in = reinterpret_cast<const unsigned long long*>(D->pmem.as<unsigned char>() + flags);
   P.counter = D->counter.as<unsigned int>();
   P.err = D->ctx->err.as<int>();
-  P.publish = D->phase + 1;
+  P.phase = reinterpret_cast<unsigned long long*>(D->counter.as<unsigned char>() + 64);
   P.timeout_ns = D->timeout_ns;
   P.nranks = D->nranks;
   P.rank = D->rank;
@@ -358,7 +368,6 @@ spmvb_status spmvb_dist_enable_peer(spmvb_dist D, void* stream) {
     SPMVB_TRY_CUDA(cudaMemcpyAsync(x_buf(D, 0), D->x_pad.get(), npad_bytes, cudaMemcpyDeviceToDevice, s));
   SPMVB_TRY_CUDA(cudaStreamSynchronize(s));
   D->cur = 0;
-  D->phase = 0;
   D->peer = true;
   return SPMVB_OK;
 }
@@ -386,8 +395,7 @@ spmvb_status spmvb_dist_set_x(spmvb_dist D, const void* h_x, void* stream) {
   // into x[cur] land, and no peer writes x[cur] before this rank's next step
   // has read it.
   if (!pad.empty()) SPMVB_TRY_CUDA(cudaMemcpyAsync(x_buf(D, D->cur), pad.data(), pad.size(), cudaMemcpyHostToDevice, s));
-  SPMVB_TRY_CUDA(cudaStreamSynchronize(s));
-  return SPMVB_OK;
+  return peer_check(D, s);
 }
 
 // One peer-exchange step. One rank: the SpMV writes the other x buffer.
@@ -406,7 +414,47 @@ static spmvb_status peer_step(spmvb_dist D, spmvb_kernel kernel, int lanes, cuda
     SPMVB_TRY(peer_launch_push(D->dtype, D->y_loc.get(), peer_view(D), D->ctx->sm_count, s));
   }
   D->cur ^= 1;
-  D->phase += 1;
+  return SPMVB_OK;
+}
+
+static bool graphs_enabled() {
+  const char* e = std::getenv("SPMVB_DIST_GRAPHS");
+  return !(e && *e == '0');
+}
+
+// The graph of two peer steps from the current parity, captured on a
+// private stream on first use (the formats are built by then: the caller ran
+// one eager step).
+static spmvb_status peer_graph(spmvb_dist D, spmvb_kernel kernel, int lanes, cudaGraphExec_t* exec, uint64_t* kernels) {
+  for (const auto& g : D->graphs)
+    if (g.kernel == kernel && g.lanes == lanes && g.parity == D->cur) {
+      *exec = g.exec;
+      *kernels = g.kernels;
+      return SPMVB_OK;
+    }
+  if (!D->capture) SPMVB_TRY_CUDA(cudaStreamCreateWithFlags(&D->capture, cudaStreamNonBlocking));
+  const int parity = D->cur;
+  const uint64_t before = spmvb_launch_count();
+  SPMVB_TRY_CUDA(cudaStreamBeginCapture(D->capture, cudaStreamCaptureModeRelaxed));
+  spmvb_status st = peer_step(D, kernel, lanes, D->capture, nullptr);
+  if (st == SPMVB_OK) st = peer_step(D, kernel, lanes, D->capture, nullptr);
+  cudaGraph_t graph = nullptr;
+  const cudaError_t e = cudaStreamEndCapture(D->capture, &graph);
+  const uint64_t captured = spmvb_launch_count() - before;
+  uncount_launch(captured);  // counted when captured, not run
+  D->cur = parity;
+  if (st != SPMVB_OK || e != cudaSuccess) {
+    if (graph) cudaGraphDestroy(graph);
+    cudaGetLastError();
+    return st != SPMVB_OK ? st : cuda_fail(e, "cudaStreamEndCapture");
+  }
+  cudaGraphExec_t ex = nullptr;
+  const cudaError_t ei = cudaGraphInstantiate(&ex, graph, 0);
+  cudaGraphDestroy(graph);
+  if (ei != cudaSuccess) return cuda_fail(ei, "cudaGraphInstantiate");
+  D->graphs.push_back({static_cast<int>(kernel), lanes, parity, ex, captured});
+  *exec = ex;
+  *kernels = captured;
   return SPMVB_OK;
 }
 
@@ -430,8 +478,23 @@ spmvb_status spmvb_dist_iterate(spmvb_dist D, spmvb_kernel kernel, int lanes, in
   DeviceGuard g(D->ctx->device);
   auto s = static_cast<cudaStream_t>(stream);
   if (D->peer) {
-    for (int it = 0; it < iters; ++it) SPMVB_TRY(peer_step(D, kernel, lanes, s, nullptr));
-    return peer_check(D, s);
+    // Asynchronous: a bounded wait that gives up is reported by the next
+    // set_x, get_x or iterate_timed. From three steps on, pairs of steps
+    // replay a captured graph.
+    int left = iters;
+    if (left >= 3 && graphs_enabled()) {
+      SPMVB_TRY(peer_step(D, kernel, lanes, s, nullptr));
+      --left;
+      cudaGraphExec_t ex = nullptr;
+      uint64_t nk = 0;
+      SPMVB_TRY(peer_graph(D, kernel, lanes, &ex, &nk));
+      for (; left >= 2; left -= 2) {
+        SPMVB_TRY_CUDA(cudaGraphLaunch(ex, s));
+        count_launch(nk);
+      }
+    }
+    for (; left > 0; --left) SPMVB_TRY(peer_step(D, kernel, lanes, s, nullptr));
+    return SPMVB_OK;
   }
   for (int it = 0; it < iters; ++it) SPMVB_TRY(dist_step(D, kernel, lanes, s));
   return SPMVB_OK;
@@ -503,6 +566,7 @@ spmvb_status spmvb_dist_get_x(spmvb_dist D, void* h_x, void* stream) {
   const void* src = D->peer ? x_buf(D, D->cur) : D->x_pad.get();
   if (!pad.empty()) SPMVB_TRY_CUDA(cudaMemcpyAsync(pad.data(), src, pad.size(), cudaMemcpyDeviceToHost, s));
   SPMVB_TRY_CUDA(cudaStreamSynchronize(s));
+  if (D->peer) SPMVB_TRY(peer_check(D, s));
   for (int r = 0; r < D->nranks; ++r) {
     const int32_t b = D->bounds[r], cnt = D->bounds[r + 1] - b;
     std::memcpy(static_cast<unsigned char*>(h_x) + size_t(b) * es, pad.data() + size_t(r) * D->max_rows * es, size_t(cnt) * es);

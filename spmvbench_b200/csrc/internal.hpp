@@ -25,6 +25,7 @@ void clear_error();
 
 extern std::atomic<uint64_t> g_launches;
 inline void count_launch(uint64_t n = 1) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+inline void uncount_launch(uint64_t n) { g_launches.fetch_sub(n, std::memory_order_relaxed); }
 
 #define SPMVB_TRY_CUDA(expr)                                  \
   do {                                                        \

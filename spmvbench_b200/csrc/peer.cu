@@ -10,10 +10,11 @@
 // kernel: CTAs count themselves finished with a gpu-scope release (their
 // stores, local and remote, ordered before it); the last one fences at
 // system scope, writes the new phase number into every other rank's counter
-// for this rank, then waits until every other rank's counter for it reaches
-// the same phase. The next kernel on the stream starts after that, so it
-// reads x with no wait of its own, and a rank stores into a peer's x buffer
-// only after that peer has finished the step that read it.
+// for this rank (its own count, kept on the device, so a captured graph of
+// steps replays unchanged), then waits until every other rank's counter for
+// it reaches the same phase. The next kernel on the stream starts after
+// that, so it reads x with no wait of its own, and a rank stores into a
+// peer's x buffer only after that peer has finished the step that read it.
 //
 //   ell_rows_peer  one launch per step: ELL rows (same order as ell_rows, so
 //                  bit-identical to csr_omp), each row's sum stored to every
@@ -87,11 +88,13 @@ __device__ void peer_arrive(const PeerView& P) {
     if (prev == gridDim.x - 1) {
       __threadfence_system();
       atomicExch(P.counter, 0u);
+      const unsigned long long phase = *P.phase + 1;
+      *P.phase = phase;
       if (ld_volatile(P.err) == 0) {
 #pragma unroll
         for (int q = 0; q < kMaxRanks; ++q)
-          if (q < P.nranks && q != P.rank) st_release_sys(P.flag_out[q], P.publish);
-        peer_wait_all(P, P.publish);
+          if (q < P.nranks && q != P.rank) st_release_sys(P.flag_out[q], phase);
+        peer_wait_all(P, phase);
       }
     }
   }

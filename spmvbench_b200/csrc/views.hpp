@@ -89,9 +89,11 @@ struct BucketView {
 // every rank's next x buffer (dst[p] already points at this rank's slice of
 // rank p's buffer; dst[rank] is its own). Phase counters: flags_in[q] is the
 // number of operations rank q has finished, written by rank q through
-// flag_out[...] of its own view. The operation's last CTA writes `publish`
-// to every other rank's counter for this rank once all of the operation's
-// stores are visible, then waits until all of this rank's counters reach it.
+// flag_out[...] of its own view; *phase is this rank's own count, kept on the
+// device so that a captured graph of steps can be replayed. The operation's
+// last CTA increments *phase, writes it to every other rank's counter for
+// this rank once all of the operation's stores are visible, then waits until
+// all of this rank's counters reach it.
 constexpr int kMaxRanks = 8;
 
 struct PeerView {
@@ -100,7 +102,7 @@ struct PeerView {
   const unsigned long long* flags_in = nullptr;  // nranks counters
   unsigned int* counter = nullptr;               // finished CTAs; 0 between launches
   int* err = nullptr;                            // context error word
-  unsigned long long publish = 0;
+  unsigned long long* phase = nullptr;
   unsigned long long timeout_ns = 0;
   int nranks = 1;
   int rank = 0;

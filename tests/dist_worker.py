@@ -34,11 +34,14 @@ for which, rows, kernel in ((2, 200000, S.ELL), (3, 300000, S.CSR_MERGE), (1, 0,
         if exchange == "peer":
             D.enable_peer()
             assert D.exchange == "peer"
-            D.set_x(x0 * 3.0)   # overwritten below: set_x must wait for no one and restart cleanly
+            D.set_x(x0 * 3.0)   # overwritten below: set_x restarts cleanly after any step count
+            D.iterate(4, kernel=kernel)   # one eager step, one replay of the 2-step graph, one eager
+            D.set_x(x0)
+            D.iterate(3, kernel=kernel)   # one eager step, one graph replay
+        else:
+            D.set_x(x0)
+            D.iterate(2, kernel=kernel)
             D.iterate(1, kernel=kernel)
-        D.set_x(x0)
-        D.iterate(2, kernel=kernel)
-        D.iterate(1, kernel=kernel)
         got = D.get_x()
         D.close()
         if kernel == S.CSR_MERGE:

@@ -131,6 +131,22 @@ def test_single_rank_peer_exchange(ctx, kernel):
             assert_bitwise(x, got, f"peer {kernel}")
     kms, sms = D.iterate_timed(2, kernel=k)
     assert 0 < kms <= sms
+    if k == S.ELL:
+        # 5 steps: one eager step, then two replays of the captured 2-step
+        # graph; every replayed kernel is counted.
+        before = S.launch_count()
+        D.iterate(5, kernel=k)
+        assert S.launch_count() - before == 5
+    x0 = S.generate_vector(81, A.n)
+    D.set_x(x0)
+    D.iterate(7, kernel=k)
+    x = x0
+    for _ in range(7):
+        x = oracle_y(A, x, S.F64, S.F64)
+    if k == S.CSR_MERGE:
+        np.testing.assert_allclose(D.get_x(), x, rtol=1e-9, atol=1e-12)
+    else:
+        assert_bitwise(x, D.get_x(), f"peer {kernel} graph")
     ctx.check()
     D.close()
 
