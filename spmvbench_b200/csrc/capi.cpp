@@ -121,7 +121,7 @@ int64_t spmvb_matrix_st::device_bytes() const {
   b += hyb_colind.bytes() + hyb_values.bytes() + hyb_rowlen.bytes() + hyb_long_rows.bytes() +
        hyb_tail_ptr.bytes() + hyb_tail_colind.bytes() + hyb_tail_values.bytes();
   for (const auto* B : {&bcsr2, &bcsr4}) b += B->rowptr.bytes() + B->colind.bytes() + B->values.bytes();
-  b += tma_rows.bytes() + merge_tile_row.bytes() + merge_carry_row.bytes() + merge_carry_val.bytes();
+  b += merge_tile_row.bytes() + merge_carry_row.bytes() + merge_carry_val.bytes();
   b += bucket_rows.bytes() + stage_in.bytes() + stage_out.bytes();
   return b;
 }

@@ -43,25 +43,6 @@ __global__ void merge_partition(CsrView A, int64_t num_items, int tile_items,
   tile_row[t] = static_cast<int>(lo);
 }
 
-__global__ void cta_row_partition(CsrView A, int G, int* __restrict__ cta_rows) {
-  const int b = blockIdx.x * blockDim.x + threadIdx.x;
-  if (b > G) return;
-  if (b == G) {
-    cta_rows[G] = A.m;
-    return;
-  }
-  const int64_t target = (static_cast<int64_t>(b) * A.nnz + G - 1) / G;
-  int lo = 0, hi = A.m;  // first row r with rowptr[r] >= target
-  while (lo < hi) {
-    const int mid = (lo + hi) >> 1;
-    if (A.rowptr[mid] < target)
-      lo = mid + 1;
-    else
-      hi = mid;
-  }
-  cta_rows[b] = lo;
-}
-
 // Copies each row's first min(len, cap) entries into column-major slots and
 // records row lengths (len, or -1 when len > cap and long_marker is set).
 template <typename W>
@@ -314,21 +295,6 @@ spmvb_status build_merge(spmvb_matrix A) {
     SPMVB_TRY_CUDA(cudaStreamSynchronize(0));
   }
   A->merge_built = true;
-  return SPMVB_OK;
-}
-
-spmvb_status build_tma(spmvb_matrix A) {
-  std::lock_guard<std::mutex> lk(A->build_mu);
-  if (A->tma_built) return SPMVB_OK;
-  DeviceGuard g(A->device);
-  const int G = std::max(1, A->ctx->sm_count * kPersistPerSm);
-  SPMVB_TRY(A->tma_rows.alloc((G + 1) * 4));
-  cta_row_partition<<<(G + 1 + 255) / 256, 256>>>(A->csr_view(), G, A->tma_rows.as<int>());
-  count_launch();
-  SPMVB_TRY_CUDA(cudaGetLastError());
-  SPMVB_TRY_CUDA(cudaStreamSynchronize(0));
-  A->tma_grid = G;
-  A->tma_built = true;
   return SPMVB_OK;
 }
 

@@ -143,11 +143,6 @@ struct spmvb_matrix_st {
     spmvb::DevBuf rowptr, colind, values;
   } bcsr2, bcsr4;
 
-  // Persistent-kernel row ranges (nnz-balanced, kPersistPerSm CTAs per SM)
-  bool tma_built = false;
-  int tma_grid = 0;
-  spmvb::DevBuf tma_rows;
-
   // Merge-path partition + carry scratch (sized for the widest accumulator)
   bool merge_built = false;
   int merge_tiles = 0;
@@ -184,10 +179,6 @@ spmvb_status build_hyb(spmvb_matrix A, int forced_k);
 spmvb_status build_bcsr(spmvb_matrix A, int block);
 spmvb_status build_merge(spmvb_matrix A);
 spmvb_status build_buckets(spmvb_matrix A);
-spmvb_status build_tma(spmvb_matrix A);
-
-// CTAs per SM of the persistent TMA-pipelined CSR kernel.
-constexpr int kPersistPerSm = 2;
 
 // Merge-path tile shape shared by the partition builder and the kernel.
 constexpr int kMergeThreads = 128;

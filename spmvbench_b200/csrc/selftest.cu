@@ -1,7 +1,8 @@
-// Failure-path self test of the bounded mbarrier wait used by the TMA
-// pipelines: one thread arms an mbarrier for 16 bytes that no copy will ever
-// deliver, waits with a short limit, records the timeout in the context's
-// error word and returns. No copy is issued, so nothing is left in flight.
+// Failure-path self test of the bounded mbarrier wait (mbar_wait in
+// common.cuh) and of the context's device error word: one thread arms an
+// mbarrier for 16 bytes that no copy will ever deliver, waits with a short
+// limit, records the timeout in the error word and returns. No copy is
+// issued, so nothing is left in flight.
 #include "internal.hpp"
 #include "common.cuh"
 

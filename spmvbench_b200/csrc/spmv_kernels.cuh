@@ -2,7 +2,7 @@
 // accumulator type Acc, like the reference kernels (src/cuda/spmv_cuda.cu).
 //
 // Kernel map (reference kernel -> this file):
-//   csr_scalar_kernel (spmv_cuda.cu:43-54)   -> csr_scalar_staged
+//   csr_scalar_kernel (spmv_cuda.cu:43-54)   -> csr_scalar_warp
 //   csr_vector_kernel (spmv_cuda.cu:56-80)   -> csr_vector<G>
 //   csr_warp_kernel   (spmv_cuda.cu:83-97)   -> csr_vector<32>
 //   csr_merge_kernel  (spmv_cuda.cu:100-125) -> csr_merge + merge_fixup (a real
@@ -11,7 +11,7 @@
 //   bcsr_kernel       (spmv_cuda.cu:145-170) -> bcsr_rows
 //   (new) hybrid ELL(K)+CSR tail            -> ell_rows<skip long> + hyb_long_rows
 //
-// Summation order. csr_scalar_staged, ell_rows and hyb's ELL part add each
+// Summation order. csr_scalar_warp, ell_rows and hyb's ELL part add each
 // row's terms left to right from zero with separately rounded multiply and
 // add, exactly as csr_omp does (src/cpu/spmv_cpu.cpp:19-25), so their output
 // is bit-identical to it. bcsr_rows follows spmv_bcsr_cpu's order
@@ -107,52 +107,6 @@ __device__ __forceinline__ void stage_products(
 }
 
 // ---------------------------------------------------------------------------
-// CSR scalar: one row per thread, csr_omp summation order, coalesced loads.
-// A CTA owns NT consecutive rows. Their nonzeros (a contiguous range of the
-// CSR arrays) are streamed through shared memory in chunks of CAP products;
-// each thread then adds its own row's products in order. A row longer than a
-// chunk simply continues its running sum across chunks.
-// ---------------------------------------------------------------------------
-template <typename T, typename Acc, int NT, int CAP>
-__global__ void __launch_bounds__(NT)
-    csr_scalar_staged(CsrView A, const T* __restrict__ x, Acc* __restrict__ y) {
-  static_assert(CAP % (NT * 4) == 0, "CAP must be a multiple of 4*NT");
-  __shared__ int s_rp[NT + 1];
-  __shared__ Acc s_prod[swz_size<Acc>(CAP)];
-  const T* __restrict__ vals = static_cast<const T*>(A.values);
-  const uint64_t ps = policy_evict_first();
-  const uint64_t pk = policy_evict_last();
-  const int t = threadIdx.x;
-  const int num_tiles = (A.m + NT - 1) / NT;
-  for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-    const int r0 = tile * NT;
-    const int nr = min(NT, A.m - r0);
-    for (int i = t; i <= nr; i += NT) s_rp[i] = A.rowptr[r0 + i];
-    __syncthreads();
-    const int64_t pbeg = s_rp[0];
-    const int64_t pend = s_rp[nr];
-    int64_t my_s = 0, my_e = 0;
-    if (t < nr) {
-      my_s = s_rp[t];
-      my_e = s_rp[t + 1];
-    }
-    Acc sum = Acc(0);
-    for (int64_t c0 = pbeg & ~int64_t(3); c0 < pend; c0 += CAP) {
-      const int64_t c1 = min(c0 + CAP, pend);
-      stage_products<T, Acc, NT, CAP / (NT * 4)>(A.colind, vals, x, c0, c1,
-                                                 s_prod, ps, pk);
-      __syncthreads();
-      const int a = static_cast<int>(max(my_s, c0) - c0);
-      const int b = static_cast<int>(min(my_e, c1) - c0);
-      for (int q = a; q < b; ++q) sum = add_rn(sum, s_prod[swz<Acc>(q)]);
-      __syncthreads();
-    }
-    if (t < nr) y[r0 + t] = sum;
-    __syncthreads();  // s_rp is rewritten by the next tile
-  }
-}
-
-// ---------------------------------------------------------------------------
 // CSR scalar, warp-staged: the kernel behind SPMVB_CSR_SCALAR.
 //
 // On B200 the random x gathers, not the matrix stream, bound short-row SpMV:
@@ -241,174 +195,6 @@ __global__ void __launch_bounds__(256)
     if (live) y[row] = sum;
   }
 }
-
-// ---------------------------------------------------------------------------
-// CSR scalar, TMA-pipelined (the B200 form of the kernel above).
-//
-// Persistent CTAs, each owning a contiguous, nnz-balanced range of rows
-// [cta_rows[b], cta_rows[b+1]) and therefore a contiguous range of the CSR
-// arrays. Thread 0 streams that range through an S-stage ring of shared
-// memory with 1-D bulk copies (cp.async.bulk, L2 evict-first), CH entries of
-// colind and values per stage, completion tracked by one mbarrier per stage.
-// Per chunk every thread forms CH/NT products (x gathered with L2
-// evict-last) into a swizzled product buffer, then walks its current row's
-// products in order: thread t owns rows R0+t, R0+t+NT, ... and keeps one
-// running sum per row across chunks, so each row is summed left to right
-// from zero exactly as csr_omp sums it. The copies of the next S-1 chunks
-// are in flight while a chunk is computed, so HBM streaming never waits on
-// the x-gather latency.
-//
-// Every mbarrier wait is bounded (kWaitLimit). The decision to give up is
-// taken CTA-wide (__syncthreads_or), the CTA then waits - bounded again - for
-// the copies it still has in flight, records the failure in *err, and
-// returns; the host reports SPMVB_ERR_TIMEOUT.
-// ---------------------------------------------------------------------------
-template <typename T, typename Acc, int CH, int S>
-struct TmaLayout {
-  static constexpr int kStageBytes = CH * 4 + CH * static_cast<int>(sizeof(T));
-  static constexpr int kProdOffset = S * kStageBytes;
-  static constexpr int kBarOffset = kProdOffset + ((swz_size<Acc>(CH) * static_cast<int>(sizeof(Acc)) + 15) / 16) * 16;
-  static constexpr int kBytes = kBarOffset + S * 8;
-};
-
-template <typename T, typename Acc, int NT, int CH, int S>
-__global__ void __launch_bounds__(NT)
-    csr_scalar_tma(CsrView A, const int* __restrict__ cta_rows, const T* __restrict__ x,
-                   Acc* __restrict__ y, int* __restrict__ err) {
-  using L = TmaLayout<T, Acc, CH, S>;
-  constexpr int GROUPS = CH / (NT * 4);
-  static_assert(CH % (NT * 4) == 0, "CH must be a multiple of 4*NT");
-  extern __shared__ __align__(128) unsigned char smem[];
-  Acc* s_prod = reinterpret_cast<Acc*>(smem + L::kProdOffset);
-  const uint32_t bar0 = smem_addr(smem + L::kBarOffset);
-  const int t = threadIdx.x;
-  const int R0 = cta_rows[blockIdx.x];
-  const int R1 = cta_rows[blockIdx.x + 1];
-  if (R0 >= R1) return;  // uniform over the CTA
-  const int64_t P0 = A.rowptr[R0];
-  const int64_t P1 = A.rowptr[R1];
-  const int64_t cbase = P0 & ~int64_t(3);
-  const int nchunks = P1 > cbase ? static_cast<int>((P1 - cbase + CH - 1) / CH) : 0;
-  const T* __restrict__ vals = static_cast<const T*>(A.values);
-  const uint64_t ps = policy_evict_first();
-  const uint64_t pk = policy_evict_last();
-
-  auto issue = [&](int stage, int chunk) {
-    const int64_t c0 = cbase + static_cast<int64_t>(chunk) * CH;
-    const int64_t left = ((P1 - c0) + 3) & ~int64_t(3);
-    const uint32_t n = static_cast<uint32_t>(left < CH ? left : CH);
-    unsigned char* st = smem + stage * L::kStageBytes;
-    const uint32_t bar = bar0 + 8u * stage;
-    mbar_expect_tx(bar, n * 4u + n * static_cast<uint32_t>(sizeof(T)));
-    bulk_g2s(smem_addr(st), A.colind + c0, n * 4u, bar, ps);
-    bulk_g2s(smem_addr(st + CH * 4), vals + c0, n * static_cast<uint32_t>(sizeof(T)), bar, ps);
-  };
-
-  if (t == 0) {
-    for (int s = 0; s < S; ++s) mbar_init(bar0 + 8u * s, 1);
-    mbar_fence_init();
-  }
-  __syncthreads();
-  if (t == 0)
-    for (int s = 0; s < S && s < nchunks; ++s) issue(s, s);
-
-  // Row state: current row and the next one (prefetched bounds).
-  int row = R0 + t;
-  bool live = row < R1;
-  int64_t rs = 0, re = 0, cur = 0, nrs = 0, nre = 0;
-  if (live) {
-    rs = A.rowptr[row];
-    re = A.rowptr[row + 1];
-    cur = rs;
-    if (row + NT < R1) {
-      nrs = A.rowptr[row + NT];
-      nre = A.rowptr[row + NT + 1];
-    }
-  }
-  Acc sum = Acc(0);
-
-  const int loops = nchunks > 0 ? nchunks : 1;
-  for (int ch = 0; ch < loops; ++ch) {
-    const int stage = ch % S;
-    const int64_t c0 = cbase + static_cast<int64_t>(ch) * CH;
-    const int64_t c1 = (c0 + CH < P1) ? c0 + CH : P1;
-    if (nchunks > 0) {
-      const bool ok = mbar_wait(bar0 + 8u * stage, static_cast<uint32_t>((ch / S) & 1));
-      if (__syncthreads_or(!ok)) {
-        if (t == 0) {
-          atomicExch(err, 1);
-          // Drain: wait (bounded) for every copy still in flight.
-          for (int c = ch; c < nchunks && c < ch + S; ++c)
-            mbar_wait(bar0 + 8u * (c % S), static_cast<uint32_t>((c / S) & 1));
-        }
-        return;
-      }
-      const unsigned char* st = smem + stage * L::kStageBytes;
-      const int* s_col = reinterpret_cast<const int*>(st);
-      const T* s_val = reinterpret_cast<const T*>(st + CH * 4);
-      const int span = static_cast<int>(c1 - c0);
-      int4 c[GROUPS];
-#pragma unroll
-      for (int g = 0; g < GROUPS; ++g) {
-        const int q = (g * NT + t) * 4;
-        c[g] = q < span ? *reinterpret_cast<const int4*>(s_col + q) : make_int4(0, 0, 0, 0);
-      }
-      T xv[GROUPS][4];
-#pragma unroll
-      for (int g = 0; g < GROUPS; ++g) {
-        const int q = (g * NT + t) * 4;
-        if (q < span) {
-          xv[g][0] = ld_keep(x + c[g].x, pk);
-          xv[g][1] = ld_keep(x + c[g].y, pk);
-          xv[g][2] = ld_keep(x + c[g].z, pk);
-          xv[g][3] = ld_keep(x + c[g].w, pk);
-        }
-      }
-#pragma unroll
-      for (int g = 0; g < GROUPS; ++g) {
-        const int q = (g * NT + t) * 4;
-        if (q < span) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) s_prod[swz<Acc>(q + i)] = prod<Acc>(s_val[q + i], xv[g][i]);
-        }
-      }
-      __syncthreads();
-    }
-    while (live) {
-      if (re <= c1) {  // the row ends in this chunk (empty rows included)
-        for (int64_t p = cur > c0 ? cur : c0; p < re; ++p)
-          sum = add_rn(sum, s_prod[swz<Acc>(static_cast<int>(p - c0))]);
-        y[row] = sum;
-        sum = Acc(0);
-        row += NT;
-        live = row < R1;
-        if (live) {
-          rs = nrs;
-          re = nre;
-          cur = rs;
-          if (row + NT < R1) {
-            nrs = A.rowptr[row + NT];
-            nre = A.rowptr[row + NT + 1];
-          }
-        }
-      } else {
-        for (int64_t p = cur > c0 ? cur : c0; p < c1; ++p)
-          sum = add_rn(sum, s_prod[swz<Acc>(static_cast<int>(p - c0))]);
-        if (c1 > cur) cur = c1;
-        break;
-      }
-    }
-    __syncthreads();  // stage `stage` and the products are no longer read
-    if (t == 0 && ch + S < nchunks) {
-      fence_proxy_async();
-      issue(stage, ch + S);
-    }
-  }
-}
-
-// nnz-balanced contiguous row ranges for the persistent kernels:
-// cta_rows[b] = lower_bound(rowptr, ceil(b * nnz / G)), cta_rows[G] = m.
-__global__ void cta_row_partition(CsrView A, int G, int* __restrict__ cta_rows);
 
 // ---------------------------------------------------------------------------
 // CSR vector: G lanes per row (G = 2..32; G = 32 is the warp kernel). Lanes

@@ -11,33 +11,11 @@
 
 namespace spmvb {
 
-constexpr int kScalarThreads = 256;
-constexpr int kScalarCap = 2048;
 constexpr int kRowThreads = 256;
-// TMA-pipelined scalar kernel: 256 threads, 2048-entry chunks, 3 stages.
-constexpr int kTmaThreads = 256;
-constexpr int kTmaChunk = 2048;
-constexpr int kTmaStages = 3;
 // BCSR: blocks requested per batch per thread.
 constexpr int kBcsrBatch = 2;
 // Warp-staged scalar kernel: entries per warp chunk.
 constexpr int kScalarWarpChunk = 512;
-
-template <typename T, typename Acc>
-static spmvb_status launch_scalar_tma(spmvb_matrix A, const T* x, Acc* y, cudaStream_t stream) {
-  using L = TmaLayout<T, Acc, kTmaChunk, kTmaStages>;
-  auto kern = csr_scalar_tma<T, Acc, kTmaThreads, kTmaChunk, kTmaStages>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    SPMVB_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
-    attr_set = true;
-  }
-  SPMVB_TRY(build_tma(A));
-  kern<<<A->tma_grid, kTmaThreads, L::kBytes, stream>>>(A->csr_view(), A->tma_rows.as<int>(), x, y,
-                                                          A->ctx->err.as<int>());
-  count_launch();
-  return SPMVB_OK;
-}
 
 template <typename T, typename Acc, int G>
 static void launch_vector(const CsrView& v, int sms, const T* x, Acc* y,
