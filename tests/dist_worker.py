@@ -19,6 +19,36 @@ rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int
 torch.cuda.set_device(local)
 dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
 ctx = S.Context(local)
+
+if len(sys.argv) > 1 and sys.argv[1] == "peer-timeout":
+    # Rank 1 skips a step (it leaves between steps, nothing in flight): rank
+    # 0's end-of-step barrier waits for a phase nobody publishes, gives up
+    # after SPMVB_PEER_TIMEOUT_MS, and the host gets SPMVB_ERR_TIMEOUT.
+    A = S.generate(2, seed=93, scale_rows=20000)
+    bounds = S.partition_rows(A.rowptr, world)
+    obj = [S.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    D = S.DistMatrix(ctx, world, rank, obj[0], A, bounds, S.F64)
+    D.enable_peer()
+    D.set_x(S.generate_vector(94, A.n))
+    status = 0
+    if rank == 0:
+        D.iterate(1, kernel=S.ELL)
+        try:
+            D.get_x()
+        except S.SpmvbError as e:
+            status = e.status
+        ctx.check()   # the error word was read and cleared; the context is usable
+        print(f"rank 0 status {status}", flush=True)
+    dist.barrier()
+    D.close()
+    # Rank 1's close still stores its last phase into rank 0's memory (rank
+    # 0, whose handle gave up, leaves its buffers allocated): rank 0 stays
+    # alive until rank 1's close has returned.
+    dist.barrier()
+    dist.destroy_process_group()
+    sys.exit(0 if rank != 0 or status == 7 else 1)
+
 bad = 0
 for which, rows, kernel in ((2, 200000, S.ELL), (3, 300000, S.CSR_MERGE), (1, 0, S.CSR_SCALAR)):
     A = S.generate(which, seed=91, scale_rows=rows)
