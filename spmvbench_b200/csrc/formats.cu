@@ -15,6 +15,7 @@
 //  buckets - SpMM row ids grouped by length (<= 8, <= 64, > 64), each group
 //          ascending, built on the host from rowptr.
 #include <algorithm>
+#include <climits>
 #include <cstring>
 #include <numeric>
 #include <string>
@@ -54,8 +55,9 @@ __global__ void ell_fill(const int* __restrict__ rowptr, const int* __restrict__
   if (r >= m) return;
   const int s = rowptr[r];
   const int len = rowptr[r + 1] - s;
-  const int take = min(len, cap);
-  rowlen[r] = (long_marker && len > cap) ? -1 : len;
+  const bool is_long = long_marker && len > cap;
+  const int take = is_long ? 0 : min(len, cap);  // long rows live whole in the CSR part
+  rowlen[r] = is_long ? -1 : len;
   for (int j = 0; j < take; ++j) {
     const int64_t p = static_cast<int64_t>(j) * m + r;
     ecol[p] = colind[s + j];
@@ -63,19 +65,19 @@ __global__ void ell_fill(const int* __restrict__ rowptr, const int* __restrict__
   }
 }
 
-// Copies entries K.. of each long row into the CSR tail (one warp per row).
+// Copies each long row whole into the CSR part (one warp per row).
 template <typename W>
 __global__ void hyb_tail_fill(const int* __restrict__ rowptr, const int* __restrict__ colind,
                               const W* __restrict__ vals, const int* __restrict__ long_rows,
-                              const int* __restrict__ tail_ptr, int n_long, int K,
+                              const int64_t* __restrict__ tail_ptr, int n_long,
                               int* __restrict__ tcol, W* __restrict__ tval) {
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x & 31;
   if (w >= n_long) return;
   const int r = long_rows[w];
-  const int s = rowptr[r] + K;
+  const int s = rowptr[r];
   const int e = rowptr[r + 1];
-  const int o = tail_ptr[w];
+  const int64_t o = tail_ptr[w];
   for (int p = s + lane; p < e; p += 32) {
     tcol[o + (p - s)] = colind[p];
     tval[o + (p - s)] = vals[p];
@@ -133,63 +135,99 @@ spmvb_status build_ell(spmvb_matrix A) {
 
 // Automatic K: the smallest width that leaves at most m/64 rows in the tail,
 // capped so the ELL part holds at most 4x the matrix's nonzeros.
-static int choose_hyb_width(const std::vector<int32_t>& rowptr, int m, int64_t nnz, int max_row) {
-  if (m == 0) return 0;
-  std::vector<int64_t> hist(static_cast<size_t>(max_row) + 2, 0);
-  for (int i = 0; i < m; ++i) hist[rowptr[i + 1] - rowptr[i]]++;
-  const int64_t allowed = std::max<int64_t>(1, m / 64);
-  int64_t longer = m - hist[0];  // rows with len > k, for k = 0
-  int K = 0;
-  while (K < max_row && longer > allowed) {
-    ++K;
-    longer -= hist[K];
-  }
-  const int cap = static_cast<int>(std::max<int64_t>(1, (4 * nnz) / m));
-  return std::min(K, cap);
+// Width of the ELL part. Heavy-tailed rows (longest > 32 x mean): K = 0,
+// every non-empty row goes to the chunked CSR part, which is balanced
+// whatever the lengths, while one thread per row would idle most lanes.
+// Otherwise K = the smallest power of two at least the mean row length.
+static int choose_hyb_width(int m, int64_t nnz, int max_row) {
+  if (m == 0 || max_row == 0) return 1;
+  const double mean = static_cast<double>(nnz) / m;
+  if (max_row > 32.0 * mean) return 0;
+  int K = 1;
+  while (K < mean && K < max_row) K <<= 1;
+  return std::min(K, max_row);
 }
 
 spmvb_status build_hyb(spmvb_matrix A, int forced_k) {
   std::lock_guard<std::mutex> lk(A->build_mu);
-  if (A->hyb_built && (forced_k <= 0 || forced_k == A->hyb_K)) return SPMVB_OK;
+  if (A->hyb_built && (forced_k == 0 || (forced_k > 0 && forced_k == A->hyb_K) || (forced_k < 0 && A->hyb_K == 0)))
+    return SPMVB_OK;
   DeviceGuard g(A->device);
   const size_t es = dtype_size(A->dtype);
-  const int K = forced_k > 0 ? std::min(forced_k, std::max(A->max_row, 1))
-                             : choose_hyb_width(A->h_rowptr, A->m, A->nnz, A->max_row);
-  std::vector<int32_t> long_rows, tail_ptr(1, 0);
+  const int K = forced_k > 0   ? std::min(forced_k, std::max(A->max_row, 1))
+                : forced_k < 0 ? 0
+                               : choose_hyb_width(A->m, A->nnz, A->max_row);
+  std::vector<int32_t> long_rows, empty_rows;
+  std::vector<int64_t> tail_ptr(1, 0);
   int64_t ell_nnz = 0;
   for (int i = 0; i < A->m; ++i) {
     const int len = A->h_rowptr[i + 1] - A->h_rowptr[i];
-    ell_nnz += std::min(len, K);
     if (len > K) {
       long_rows.push_back(i);
-      tail_ptr.push_back(tail_ptr.back() + (len - K));
+      tail_ptr.push_back(tail_ptr.back() + len);
+    } else {
+      ell_nnz += len;
+      if (K == 0) empty_rows.push_back(i);
     }
   }
+  const int n_long = static_cast<int>(long_rows.size());
   const int64_t slots = static_cast<int64_t>(A->m) * K;
   const int64_t tail = tail_ptr.back();
+  // Chunks of kHybChunk entries of the CSR part: the slot of the row holding
+  // each chunk's first entry; the rows spanning more than one chunk, and
+  // which of them each chunk holds first / last.
+  const int64_t n_chunks64 = (tail + kHybChunk - 1) / kHybChunk;
+  if (n_chunks64 > INT32_MAX / 2) return fail(SPMVB_ERR_UNSUPPORTED, "HYB: too many long-row entries");
+  const int n_chunks = static_cast<int>(n_chunks64);
+  std::vector<int32_t> chunk_row(static_cast<size_t>(n_chunks) + 1), split_rows;
+  std::vector<int32_t> first_split(std::max(n_chunks, 1), -1), last_split(std::max(n_chunks, 1), -1);
+  for (int c = 0, li = 0; c < n_chunks; ++c) {
+    const int64_t pos = static_cast<int64_t>(c) * kHybChunk;
+    while (tail_ptr[li + 1] <= pos) ++li;
+    chunk_row[c] = li;
+  }
+  chunk_row[n_chunks] = n_long;
+  for (int li = 0; li < n_long; ++li) {
+    const int64_t ca = tail_ptr[li] / kHybChunk, cb = (tail_ptr[li + 1] - 1) / kHybChunk;
+    if (ca == cb) continue;
+    const int si = static_cast<int>(split_rows.size());
+    split_rows.push_back(li);
+    last_split[ca] = si;
+    for (int64_t c = ca + 1; c <= cb; ++c) first_split[c] = si;
+  }
+
   SPMVB_TRY(check_fits(A, static_cast<double>(slots + tail) * (4 + es) + 8.0 * A->m, "HYB"));
   SPMVB_TRY(A->hyb_colind.alloc(std::max<int64_t>(slots, 1) * 4));
   SPMVB_TRY(A->hyb_values.alloc(std::max<int64_t>(slots, 1) * es));
   SPMVB_TRY(A->hyb_rowlen.alloc(std::max<int64_t>(A->m, 1) * 4));
   SPMVB_TRY(upload(A->hyb_long_rows, long_rows.data(), long_rows.size() * 4, std::max<size_t>(long_rows.size(), 1) * 4));
-  SPMVB_TRY(upload(A->hyb_tail_ptr, tail_ptr.data(), tail_ptr.size() * 4, tail_ptr.size() * 4));
+  SPMVB_TRY(upload(A->hyb_tail_ptr, tail_ptr.data(), tail_ptr.size() * 8, tail_ptr.size() * 8));
   SPMVB_TRY(A->hyb_tail_colind.alloc((tail + kPad) * 4));
   SPMVB_TRY(A->hyb_tail_values.alloc((tail + kPad) * es));
+  SPMVB_TRY(upload(A->hyb_chunk_row, chunk_row.data(), chunk_row.size() * 4, chunk_row.size() * 4));
+  SPMVB_TRY(upload(A->hyb_first_split, first_split.data(), first_split.size() * 4, first_split.size() * 4));
+  SPMVB_TRY(upload(A->hyb_last_split, last_split.data(), last_split.size() * 4, last_split.size() * 4));
+  SPMVB_TRY(upload(A->hyb_split_rows, split_rows.data(), split_rows.size() * 4, std::max<size_t>(split_rows.size(), 1) * 4));
+  SPMVB_TRY(A->hyb_split_count.alloc(std::max<size_t>(split_rows.size(), 1) * 4));  // zero-filled
+  SPMVB_TRY(upload(A->hyb_empty_rows, empty_rows.data(), empty_rows.size() * 4, std::max<size_t>(empty_rows.size(), 1) * 4));
+  SPMVB_TRY(A->hyb_partial_first.alloc(std::max<size_t>(n_chunks, 1) * 8));
+  SPMVB_TRY(A->hyb_partial_last.alloc(std::max<size_t>(n_chunks, 1) * 8));
   if (A->m > 0) {
-    if (es == 8)
-      launch_ell_fill<unsigned long long>(A, K, true, A->hyb_colind.as<int>(), A->hyb_values.get(), A->hyb_rowlen.as<int>());
-    else
-      launch_ell_fill<unsigned int>(A, K, true, A->hyb_colind.as<int>(), A->hyb_values.get(), A->hyb_rowlen.as<int>());
-    const int n_long = static_cast<int>(long_rows.size());
+    if (K > 0) {
+      if (es == 8)
+        launch_ell_fill<unsigned long long>(A, K, true, A->hyb_colind.as<int>(), A->hyb_values.get(), A->hyb_rowlen.as<int>());
+      else
+        launch_ell_fill<unsigned int>(A, K, true, A->hyb_colind.as<int>(), A->hyb_values.get(), A->hyb_rowlen.as<int>());
+    }
     if (n_long > 0) {
       const int grid = (n_long + 7) / 8;
       if (es == 8)
         hyb_tail_fill<unsigned long long><<<grid, 256>>>(A->rowptr.as<int>(), A->colind.as<int>(), A->values.as<unsigned long long>(),
-                                                         A->hyb_long_rows.as<int>(), A->hyb_tail_ptr.as<int>(), n_long, K,
+                                                         A->hyb_long_rows.as<int>(), A->hyb_tail_ptr.as<int64_t>(), n_long,
                                                          A->hyb_tail_colind.as<int>(), A->hyb_tail_values.as<unsigned long long>());
       else
         hyb_tail_fill<unsigned int><<<grid, 256>>>(A->rowptr.as<int>(), A->colind.as<int>(), A->values.as<unsigned int>(),
-                                                   A->hyb_long_rows.as<int>(), A->hyb_tail_ptr.as<int>(), n_long, K,
+                                                   A->hyb_long_rows.as<int>(), A->hyb_tail_ptr.as<int64_t>(), n_long,
                                                    A->hyb_tail_colind.as<int>(), A->hyb_tail_values.as<unsigned int>());
       count_launch();
     }
@@ -199,7 +237,10 @@ spmvb_status build_hyb(spmvb_matrix A, int forced_k) {
   A->hyb_K = K;
   A->hyb_ell_nnz = ell_nnz;
   A->hyb_tail_nnz = tail;
-  A->hyb_n_long = static_cast<int>(long_rows.size());
+  A->hyb_n_long = n_long;
+  A->hyb_n_chunks = n_chunks;
+  A->hyb_n_split = static_cast<int>(split_rows.size());
+  A->hyb_n_empty = static_cast<int>(empty_rows.size());
   A->hyb_built = true;
   return SPMVB_OK;
 }

@@ -132,8 +132,12 @@ struct spmvb_matrix_st {
   int hyb_K = 0;
   int64_t hyb_ell_nnz = 0, hyb_tail_nnz = 0;
   int hyb_n_long = 0;
+  int hyb_n_chunks = 0;
+  int hyb_n_split = 0;
+  int hyb_n_empty = 0;
   spmvb::DevBuf hyb_colind, hyb_values, hyb_rowlen, hyb_long_rows, hyb_tail_ptr,
-      hyb_tail_colind, hyb_tail_values;
+      hyb_tail_colind, hyb_tail_values, hyb_chunk_row, hyb_first_split, hyb_last_split,
+      hyb_split_rows, hyb_split_count, hyb_empty_rows, hyb_partial_first, hyb_partial_last;
 
   // BCSR 2x2 and 4x4
   struct Bcsr {

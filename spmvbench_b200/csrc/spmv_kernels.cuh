@@ -9,7 +9,7 @@
 //                                              merge-path, not a row queue)
 //   ell_kernel        (spmv_cuda.cu:128-142) -> ell_rows
 //   bcsr_kernel       (spmv_cuda.cu:145-170) -> bcsr_rows
-//   (new) hybrid ELL(K)+CSR tail            -> ell_rows<skip long> + hyb_long_rows
+//   (new) hybrid ELL(K)+CSR                 -> hyb_rows
 //
 // Summation order. csr_scalar_warp, ell_rows and hyb's ELL part add each
 // row's terms left to right from zero with separately rounded multiply and
@@ -437,32 +437,148 @@ __global__ void __launch_bounds__(256)
   y[row] = ell_row_sum<T, Acc>(E, row, L, x, policy_evict_first(), policy_evict_last());
 }
 
-// Hybrid long rows: one warp per row over its K ELL slots and its CSR tail.
+// Hybrid ELL(K) + CSR, one launch (see HybView for the layout).
+//
+// ELL blocks: one thread per row with len <= K, csr_omp order (bit-identical).
+//
+// Chunk blocks: the long rows are streamed in chunks of kHybChunk entries, one
+// warp per chunk, so every warp gets the same number of entries whatever the
+// row lengths. Lane l loads entries l, l+32, ... of its chunk (coalesced),
+// every gather of the chunk is in flight before any product is formed. A
+// chunk inside one row is reduced by the warp in a fixed order (lane partials
+// over p = l + 32i, then a butterfly); otherwise the products go to the warp's
+// slice of shared memory and lane l sums the pieces of rows li0+l, li0+l+32,
+// ... left to right. A row wholly inside the chunk is written to y; a piece
+// of a split row goes to partial_last / partial_first, and the warp whose
+// piece completes a split row (per-row counter) adds its pieces in a fixed
+// order: partial_last of its first chunk, then the partial_first of the later
+// ones (lane partials, butterfly). Deterministic; long rows are re-associated
+// (bounded by 2*gamma_n*sum|a_ij x_j|).
+//
+// Remaining blocks: y = 0 for the empty rows when K = 0.
+template <typename Acc>
+__device__ __forceinline__ void hyb_finish_split(const HybView& H, int si, Acc* __restrict__ y, int lane) {
+  const int li = H.split_rows[si];
+  const int ca = static_cast<int>(H.tail_ptr[li] / kHybChunk);
+  const int cb = static_cast<int>((H.tail_ptr[li + 1] - 1) / kHybChunk);
+  const Acc* pf = static_cast<const Acc*>(H.partial_first);
+  const Acc* pl = static_cast<const Acc*>(H.partial_last);
+  Acc v = Acc(0);
+  for (int c = ca + 1 + lane; c <= cb; c += kWarp) v = add_rn(v, __ldcg(pf + c));
+  v = group_sum<kWarp>(v);
+  if (lane == 0) {
+    y[H.long_rows[li]] = add_rn(__ldcg(pl + ca), v);
+    H.split_count[si] = 0;  // ready for the next launch
+  }
+}
+
 template <typename T, typename Acc>
 __global__ void __launch_bounds__(256)
-    hyb_long_rows(HybView H, const T* __restrict__ x, Acc* __restrict__ y) {
-  const int w = (blockIdx.x * blockDim.x + threadIdx.x) / kWarp;
-  const int lane = threadIdx.x & (kWarp - 1);
-  if (w >= H.n_long) return;
+    hyb_rows(HybView H, const T* __restrict__ x, Acc* __restrict__ y) {
+  constexpr int W = 256 / kWarp;
+  constexpr int PER = kHybChunk / kWarp;
+  __shared__ Acc s_prod[W][kHybChunk];
   const uint64_t ps = policy_evict_first();
   const uint64_t pk = policy_evict_last();
-  const int row = H.long_rows[w];
-  const T* __restrict__ ev = static_cast<const T*>(H.ell.values);
-  const T* __restrict__ tv = static_cast<const T*>(H.tail_values);
-  Acc sum = Acc(0);
-  for (int j = lane; j < H.ell.width; j += kWarp) {
-    const int64_t p = static_cast<int64_t>(j) * H.ell.ld + row;
-    sum = add_rn(sum, prod<Acc>(ld_stream(ev + p, ps),
-                                ld_keep(x + ld_stream(H.ell.colind + p, ps), pk)));
+  if (static_cast<int>(blockIdx.x) < H.ell_blocks) {
+    const int row = blockIdx.x * blockDim.x + threadIdx.x;
+    if (row < H.ell.m) {
+      const int L = H.ell.row_lengths[row];
+      if (L >= 0) y[row] = ell_row_sum<T, Acc>(H.ell, row, L, x, ps, pk);
+    }
+    return;
   }
-  const int s = H.tail_ptr[w];
-  const int e = H.tail_ptr[w + 1];
-#pragma unroll 4
-  for (int p = s + lane; p < e; p += kWarp)
-    sum = add_rn(sum, prod<Acc>(ld_stream(tv + p, ps),
-                                ld_keep(x + ld_stream(H.tail_colind + p, ps), pk)));
-  sum = group_sum<kWarp>(sum);
-  if (lane == 0) y[row] = sum;
+  const int cb_index = static_cast<int>(blockIdx.x) - H.ell_blocks;
+  if (cb_index >= H.chunk_blocks) {
+    const int i = (cb_index - H.chunk_blocks) * blockDim.x + threadIdx.x;
+    if (i < H.n_empty) y[H.empty_rows[i]] = Acc(0);
+    return;
+  }
+  const int wib = threadIdx.x / kWarp;
+  const int lane = threadIdx.x & (kWarp - 1);
+  const int c = cb_index * W + wib;
+  if (c >= H.n_chunks) return;
+  const T* __restrict__ tv = static_cast<const T*>(H.tail_values);
+  const int64_t c0 = static_cast<int64_t>(c) * kHybChunk;
+  const int64_t c1 = min(c0 + kHybChunk, H.tail_nnz);
+  const int li0 = H.chunk_row[c];
+  const int nxt = H.chunk_row[c + 1];
+  const int li1 = (H.tail_ptr[nxt] == c1) ? nxt - 1 : nxt;  // row holding entry c1 - 1
+  Acc* __restrict__ pf = static_cast<Acc*>(H.partial_first);
+  Acc* __restrict__ pl = static_cast<Acc*>(H.partial_last);
+
+  int col[PER];
+  T val[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int64_t p = c0 + lane + i * kWarp;
+    col[i] = p < c1 ? ld_stream(H.tail_colind + p, ps) : 0;
+    val[i] = p < c1 ? ld_stream(tv + p, ps) : T(0);
+  }
+  Acc pr[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i)
+    pr[i] = (c0 + lane + i * kWarp < c1) ? prod<Acc>(val[i], ld_keep(x + col[i], pk)) : Acc(0);
+
+  // A lane can complete at most two split rows: the chunk's first row
+  // (through partial_first) and its last row (through partial_last).
+  int fin_first = -1, fin_last = -1;
+  auto completes = [&](int si) -> bool {
+    __threadfence();  // the partial is visible before the count
+    const int li = H.split_rows[si];
+    const int pieces = static_cast<int>((H.tail_ptr[li + 1] - 1) / kHybChunk - H.tail_ptr[li] / kHybChunk) + 1;
+    return atomicAdd(H.split_count + si, 1) == pieces - 1;
+  };
+  if (li0 == li1) {
+    Acc v = Acc(0);
+#pragma unroll
+    for (int i = 0; i < PER; ++i) v = add_rn(v, pr[i]);  // entries past c1 add exact zeros
+    v = group_sum<kWarp>(v);
+    if (lane == 0) {
+      const int64_t rs = H.tail_ptr[li0], re = H.tail_ptr[li0 + 1];
+      if (rs < c0) {
+        pf[c] = v;
+        if (completes(H.first_split[c])) fin_first = H.first_split[c];
+      } else if (re > c1) {
+        pl[c] = v;
+        if (completes(H.last_split[c])) fin_last = H.last_split[c];
+      } else {
+        y[H.long_rows[li0]] = v;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) s_prod[wib][lane + i * kWarp] = pr[i];
+    __syncwarp();
+    for (int li = li0 + lane; li <= li1; li += kWarp) {
+      const int64_t rs = H.tail_ptr[li], re = H.tail_ptr[li + 1];
+      const int a = static_cast<int>(max(rs, c0) - c0);
+      const int b = static_cast<int>(min(re, c1) - c0);
+      Acc v = Acc(0);
+      for (int q = a; q < b; ++q) v = add_rn(v, s_prod[wib][q]);
+      if (rs < c0) {
+        pf[c] = v;
+        if (completes(H.first_split[c])) fin_first = H.first_split[c];
+      } else if (re > c1) {
+        pl[c] = v;
+        if (completes(H.last_split[c])) fin_last = H.last_split[c];
+      } else {
+        y[H.long_rows[li]] = v;
+      }
+    }
+  }
+  // The warp finishes the split rows whose last piece it wrote.
+  for (int k = 0; k < 2; ++k) {
+    const int mine = k == 0 ? fin_first : fin_last;
+    unsigned todo = __ballot_sync(0xffffffffu, mine >= 0);
+    while (todo) {
+      const int src = __ffs(todo) - 1;
+      todo &= todo - 1;
+      const int si = __shfl_sync(0xffffffffu, mine, src);
+      __threadfence();
+      hyb_finish_split<Acc>(H, si, y, lane);
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------

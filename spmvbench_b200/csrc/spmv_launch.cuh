@@ -98,15 +98,28 @@ spmvb_status launch_spmv(spmvb_matrix A, spmvb_kernel kernel, int lanes,
       h.ell.width = A->hyb_K;
       h.ell.ld = A->m;
       h.long_rows = A->hyb_long_rows.as<int>();
-      h.tail_ptr = A->hyb_tail_ptr.as<int>();
+      h.tail_ptr = A->hyb_tail_ptr.as<int64_t>();
       h.tail_colind = A->hyb_tail_colind.as<int>();
       h.tail_values = A->hyb_tail_values.get();
+      h.chunk_row = A->hyb_chunk_row.as<int>();
+      h.first_split = A->hyb_first_split.as<int>();
+      h.last_split = A->hyb_last_split.as<int>();
+      h.split_rows = A->hyb_split_rows.as<int>();
+      h.split_count = A->hyb_split_count.as<int>();
+      h.empty_rows = A->hyb_empty_rows.as<int>();
+      h.partial_first = A->hyb_partial_first.get();
+      h.partial_last = A->hyb_partial_last.get();
+      h.tail_nnz = A->hyb_tail_nnz;
       h.n_long = A->hyb_n_long;
-      ell_rows<T, Acc, true><<<(A->m + kRowThreads - 1) / kRowThreads, kRowThreads, 0, stream>>>(h.ell, x, y);
-      count_launch();
-      if (h.n_long > 0) {
-        const int warps_per_block = kRowThreads / kWarp;
-        hyb_long_rows<T, Acc><<<(h.n_long + warps_per_block - 1) / warps_per_block, kRowThreads, 0, stream>>>(h, x, y);
+      h.n_chunks = A->hyb_n_chunks;
+      h.n_split = A->hyb_n_split;
+      h.n_empty = A->hyb_n_empty;
+      h.ell_blocks = A->hyb_K > 0 ? (A->m + kRowThreads - 1) / kRowThreads : 0;
+      h.chunk_blocks = (h.n_chunks + kRowThreads / kWarp - 1) / (kRowThreads / kWarp);
+      const int empty_blocks = (h.n_empty + kRowThreads - 1) / kRowThreads;
+      const int grid = h.ell_blocks + h.chunk_blocks + empty_blocks;
+      if (grid > 0) {
+        hyb_rows<T, Acc><<<grid, kRowThreads, 0, stream>>>(h, x, y);
         count_launch();
       }
       break;

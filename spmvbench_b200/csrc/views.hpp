@@ -35,17 +35,42 @@ struct EllView {
   int64_t ld = 0;
 };
 
-// Hybrid ELL(K) + CSR tail. Every row keeps its first min(len, K) entries in
-// the column-major ELL part; rows longer than K ("long rows") keep the rest
-// in a CSR tail indexed by long-row slot. The ELL kernel writes rows with
-// len <= K (hyb_len[i] >= 0); the long-row kernel writes the others.
+// Hybrid ELL(K) + CSR. Rows with len <= K keep their entries in the
+// column-major ELL part (row_lengths = len); rows longer than K ("long rows",
+// row_lengths = -1) are stored whole, back to back, in a CSR part indexed by
+// long-row slot, streamed in equal chunks of kHybChunk entries. chunk_row[c]
+// is the slot of the row holding entry c*kHybChunk (chunk_row[n_chunks] =
+// n_long). Rows spanning more than one chunk ("split rows", slots in
+// split_rows) leave one partial per chunk: partial_last[c] for the chunk
+// where the row starts, partial_first[c] for every later chunk it reaches;
+// first_split[c] / last_split[c] name the split row whose piece chunk c
+// holds first / last (-1: none), and split_count[s] counts the pieces
+// written (0 between launches). With K = 0 the empty rows are listed in
+// empty_rows. One launch: ell_blocks blocks of ELL rows, chunk_blocks blocks
+// of chunks, then the empty rows.
+constexpr int kHybChunk = 256;
+
 struct HybView {
-  EllView ell;                 // width K; row_lengths = len, or -1 for long rows
+  EllView ell;                      // width K
   const int* long_rows = nullptr;   // n_long row ids, ascending
-  const int* tail_ptr = nullptr;    // n_long + 1 offsets into the tail
-  const int* tail_colind = nullptr; // + kPad
+  const int64_t* tail_ptr = nullptr;  // n_long + 1 offsets into the CSR part
+  const int* tail_colind = nullptr;   // + kPad
   const void* tail_values = nullptr;
+  const int* chunk_row = nullptr;     // n_chunks + 1
+  const int* first_split = nullptr;   // n_chunks
+  const int* last_split = nullptr;    // n_chunks
+  const int* split_rows = nullptr;    // n_split
+  int* split_count = nullptr;         // n_split
+  const int* empty_rows = nullptr;    // n_empty (K = 0 only)
+  void* partial_first = nullptr;      // n_chunks
+  void* partial_last = nullptr;       // n_chunks
+  int64_t tail_nnz = 0;
   int n_long = 0;
+  int n_chunks = 0;
+  int n_split = 0;
+  int n_empty = 0;
+  int ell_blocks = 0;
+  int chunk_blocks = 0;
 };
 
 // Blocked CSR with R x C row-major blocks (src/formats.cpp:45-105 layout).

@@ -189,3 +189,45 @@ def test_host_buffer_entry_point_matches_device(ctx):
     M = S.DeviceMatrix(ctx, A, S.F64)
     for kernel in (S.CSR_SCALAR, S.CSR_MERGE, S.ELL):
         assert_bitwise(run_spmv(M, x, kernel), M.spmv_host(x, kernel=kernel), "host entry")
+
+
+@pytest.mark.parametrize("K", [-1, 1, 3, 8, 64, 257])
+def test_hyb_widths_are_exact_bounded_and_deterministic(ctx, K):
+    """Every width of the hybrid format (-1 = width 0: every row chunked):
+    rows up to K bit-identical to csr_omp, long rows (chunked, some split
+    across chunks) within the gamma_n bound, and the same bits on every
+    rerun (the split rows' counters reset themselves)."""
+    A = S.generate(3, seed=57, scale_rows=150000)
+    x = S.generate_vector(58, A.n)
+    M = S.DeviceMatrix(ctx, A, S.F64)
+    M.prepare(S.HYB, K)
+    info = M.info()
+    K = max(K, 0)
+    assert info["hyb_width"] == K
+    lens = np.diff(A.rowptr)
+    assert info["hyb_long_rows"] == int((lens > K).sum())
+    assert info["hyb_tail_nnz"] == int(lens[lens > K].sum())
+    assert info["hyb_ell_nnz"] == int(lens[lens <= K].sum())
+    check_variant(ctx, A, x, S.F64, S.F64, S.HYB, 1, 4, "hyb", f"hyb K={K}", M)
+    a = run_spmv(M, x, S.HYB)
+    for _ in range(2):
+        assert_bitwise(a, run_spmv(M, x, S.HYB), "hyb rerun")
+
+
+@pytest.mark.parametrize("dtype,acc", DTYPE_PAIRS)
+def test_hyb_width_zero_writes_empty_rows(ctx, dtype, acc):
+    """Width 0 lists the empty rows and writes their zeros in the same
+    launch; every other row goes through the chunks."""
+    B = S.generate(3, seed=59, scale_rows=60000)
+    lens = np.diff(B.rowptr)
+    lens[::7] = 0  # every 7th row emptied
+    rowptr = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    keep = np.repeat(np.arange(B.m) % 7 != 0, np.diff(B.rowptr))
+    A = S.CsrMatrix(B.m, B.n, rowptr, B.colind[keep], B.values[keep])
+    x = S.generate_vector(60, A.n)
+    M = S.DeviceMatrix(ctx, A, dtype)
+    M.prepare(S.HYB, -1)
+    assert M.info()["hyb_width"] == 0 and M.info()["hyb_long_rows"] == int((lens > 0).sum())
+    y = run_spmv(M, x, S.HYB, acc=acc)
+    assert np.all(y[::7] == 0.0)
+    assert_rows_within_bound(A, x, oracle_y(A, x, dtype, acc), y, dtype, acc, "hyb K=0")
