@@ -41,7 +41,8 @@ typedef enum spmvb_status {
   SPMVB_ERR_CUDA = 5,             /* CUDA runtime error (message attached) */
   SPMVB_ERR_NCCL = 6,             /* NCCL error (message attached)         */
   SPMVB_ERR_TIMEOUT = 7,          /* a bounded wait gave up                */
-  SPMVB_ERR_NO_DEVICE = 8         /* no CUDA device / bad device ordinal   */
+  SPMVB_ERR_NO_DEVICE = 8,        /* no CUDA device / bad device ordinal   */
+  SPMVB_ERR_IO = 9                /* a file cannot be opened, read, written */
 } spmvb_status;
 
 typedef enum spmvb_dtype { SPMVB_F32 = 0, SPMVB_F64 = 1 } spmvb_dtype;
@@ -286,6 +287,33 @@ spmvb_status spmvb_generate(int which, uint64_t seed, int32_t scale_rows,
                             double* h_values);
 /* x_i ~ U(-1,1) from a seeded 64-bit generator, shared by oracle and GPU. */
 spmvb_status spmvb_generate_vector(uint64_t seed, int64_t len, double* h_out);
+
+/* ---- input formats ------------------------------------------------------------- */
+/* Host CSR read from a file (f64 values; a caller wanting f32 converts with
+ * round-to-nearest, as the reference's static_cast<float> does). */
+typedef struct spmvb_host_csr_st* spmvb_host_csr;
+/* Replaces read_matrix_market<T> (src/mtx_io.cpp:40-172, declared in
+ * include/spmvbench/mtx_io.hpp): coordinate real / integer / pattern,
+ * general / symmetric; the same CSR (rows sorted by column with the
+ * reference's sort, so repeated entries keep its order) and the same error
+ * texts ("Matrix Market: <path>: ..."; SPMVB_ERR_IO when the file cannot be
+ * opened, SPMVB_ERR_INVALID_MATRIX for a malformed file). The entry lines are
+ * parsed by `threads` threads (0 = all hardware threads). */
+spmvb_status spmvb_read_matrix_market(const char* path, int threads,
+                                      spmvb_host_csr* out);
+/* Binary CSR cache (no reference counterpart): a 40-byte header ("SPMVBCSR",
+ * version 1, value bytes 8, m, n, nnz) then rowptr, colind, f64 values. The
+ * CSR is validated on write and on read. */
+spmvb_status spmvb_csr_cache_write(const char* path, int32_t m, int32_t n,
+                                   int64_t nnz, const int32_t* h_rowptr,
+                                   const int32_t* h_colind,
+                                   const double* h_values);
+spmvb_status spmvb_csr_cache_read(const char* path, spmvb_host_csr* out);
+/* Sizes and pointers into the handle's arrays (valid until it is freed). */
+spmvb_status spmvb_host_csr_get(spmvb_host_csr A, int32_t* m, int32_t* n,
+                                int64_t* nnz, const int32_t** rowptr,
+                                const int32_t** colind, const double** values);
+void spmvb_host_csr_free(spmvb_host_csr A);
 
 /* ---- multi-GPU row sharding ---------------------------------------------------- */
 /* nnz-balanced contiguous row blocks: bounds[g] = lower_bound(rowptr,

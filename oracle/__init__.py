@@ -90,6 +90,25 @@ def ref() -> C.CDLL:
     return _ref
 
 
+def ref_read_matrix_market(path: str):
+    """The reference's read_matrix_market<double> (src/mtx_io.cpp:40-172),
+    run from oracle/_ref: (m, n, rowptr, colind, values), or RuntimeError
+    with the reference's message."""
+    lib = ref()
+    err = C.create_string_buffer(1024)
+    h = lib.ref_read_mtx_d(os.fsencode(path), err, 1024)
+    if not h:
+        raise RuntimeError(err.value.decode(errors="replace"))
+    m, n, nnz = C.c_int32(), C.c_int32(), C.c_int64()
+    lib.ref_csr_shape_d(h, C.byref(m), C.byref(n), C.byref(nnz))
+    rp = np.zeros(m.value + 1, np.int32)
+    ci = np.zeros(max(nnz.value, 1), np.int32)
+    va = np.zeros(max(nnz.value, 1), np.float64)
+    lib.ref_csr_arrays_d(h, _p(rp), _p(ci), _p(va))
+    lib.ref_csr_destroy_d(h)
+    return m.value, n.value, rp, ci[:nnz.value], va[:nnz.value]
+
+
 _SUF = {(np.float64, np.float64): "dd", (np.float32, np.float32): "ff", (np.float32, np.float64): "fd"}
 
 

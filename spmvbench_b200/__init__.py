@@ -10,6 +10,7 @@ reference's CsrMatrix<T> (include/spmvbench/csr.hpp:16-35).
 from __future__ import annotations
 
 import ctypes as C
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -20,6 +21,7 @@ from ._lib import (BCSR, CSR_MERGE, CSR_SCALAR, CSR_VECTOR, CSR_WARP, ELL, F32, 
 
 __all__ = [
     "CsrMatrix", "Context", "DeviceMatrix", "DistMatrix", "SpmvbError", "generate",
+    "read_matrix_market", "write_csr_cache", "read_csr_cache",
     "generate_vector", "row_stats", "choose_spmv", "choose_spmv_reference", "partition_rows",
     "launch_count", "gpu_available", "csr_validate", "shard_csr", "query_gpu", "kernel_name", "nccl_unique_id",
     "CSR_SCALAR", "CSR_VECTOR", "CSR_WARP", "CSR_MERGE", "ELL", "BCSR", "HYB", "F32", "F64",
@@ -73,6 +75,48 @@ def generate(which: int, seed: int = 2024, scale_rows: int = 0) -> CsrMatrix:
                                   _ptr(rowptr), colind.ctypes.data_as(C.c_void_p),
                                   values.ctypes.data_as(C.c_void_p)), "spmvb_generate")
     return CsrMatrix(m.value, n.value, rowptr, colind[:nnz.value], values[:nnz.value])
+
+
+def _take_host_csr(h) -> CsrMatrix:
+    """Copies a spmvb_host_csr handle into a CsrMatrix and frees it."""
+    lib = load()
+    try:
+        m, n, nnz = C.c_int32(), C.c_int32(), C.c_int64()
+        rp, ci, va = C.c_void_p(), C.c_void_p(), C.c_void_p()
+        call("spmvb_host_csr_get", h, C.byref(m), C.byref(n), C.byref(nnz), C.byref(rp), C.byref(ci), C.byref(va))
+
+        def arr(ptr, count, ctype, dtype):
+            if count == 0:
+                return np.zeros(0, dtype)
+            return np.ctypeslib.as_array(C.cast(ptr, C.POINTER(ctype)), shape=(count,)).copy()
+
+        return CsrMatrix(m.value, n.value, arr(rp, m.value + 1, C.c_int32, np.int32),
+                         arr(ci, nnz.value, C.c_int32, np.int32), arr(va, nnz.value, C.c_double, np.float64))
+    finally:
+        lib.spmvb_host_csr_free(h)
+
+
+def read_matrix_market(path: str, threads: int = 0) -> CsrMatrix:
+    """The reference's read_matrix_market (same CSR, same errors), parsed by
+    `threads` threads (0 = all). fp64 values; .astype(np.float32) gives the
+    reference's read_matrix_market<float>."""
+    h = C.c_void_p()
+    call("spmvb_read_matrix_market", os.fsencode(path), threads, C.byref(h))
+    return _take_host_csr(h)
+
+
+def write_csr_cache(path: str, A: CsrMatrix) -> None:
+    """Binary CSR cache of A (validated), read back by read_csr_cache."""
+    rp = np.ascontiguousarray(A.rowptr, np.int32)
+    ci = np.ascontiguousarray(A.colind, np.int32)
+    va = np.ascontiguousarray(A.values, np.float64)
+    call("spmvb_csr_cache_write", os.fsencode(path), A.m, A.n, A.nnz, _ptr(rp), _ptr(ci), _ptr(va))
+
+
+def read_csr_cache(path: str) -> CsrMatrix:
+    h = C.c_void_p()
+    call("spmvb_csr_cache_read", os.fsencode(path), C.byref(h))
+    return _take_host_csr(h)
 
 
 def generate_vector(seed: int, n: int) -> np.ndarray:

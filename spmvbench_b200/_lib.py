@@ -16,7 +16,7 @@ LIB_PATH = os.path.join(_HERE, "lib", "libspmvb.so")
 OK = 0
 STATUS = {
     0: "ok", 1: "invalid argument", 2: "invalid matrix", 3: "unsupported",
-    4: "out of memory", 5: "CUDA error", 6: "NCCL error", 7: "timeout", 8: "no device",
+    4: "out of memory", 5: "CUDA error", 6: "NCCL error", 7: "timeout", 8: "no device", 9: "i/o error",
 }
 
 F32, F64 = 0, 1
@@ -117,6 +117,11 @@ SIGNATURES = {
     "spmvb_dist_enable_peer": (C.c_int, [P, P]),
     "spmvb_dist_exchange": (C.c_int, [P]),
     "spmvb_dist_get_info": (C.c_int, [P, I32P, I32P, I32P, I64P]),
+    "spmvb_read_matrix_market": (C.c_int, [C.c_char_p, C.c_int, C.POINTER(P)]),
+    "spmvb_csr_cache_write": (C.c_int, [C.c_char_p, C.c_int32, C.c_int32, C.c_int64, P, P, P]),
+    "spmvb_csr_cache_read": (C.c_int, [C.c_char_p, C.POINTER(P)]),
+    "spmvb_host_csr_get": (C.c_int, [P, I32P, I32P, I64P, C.POINTER(P), C.POINTER(P), C.POINTER(P)]),
+    "spmvb_host_csr_free": (None, [P]),
 }
 
 _lib = None

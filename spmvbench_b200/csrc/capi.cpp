@@ -145,6 +145,7 @@ const char* spmvb_status_string(spmvb_status s) {
     case SPMVB_ERR_NCCL: return "NCCL error";
     case SPMVB_ERR_TIMEOUT: return "timeout";
     case SPMVB_ERR_NO_DEVICE: return "no device";
+    case SPMVB_ERR_IO: return "i/o error";
   }
   return "unknown status";
 }

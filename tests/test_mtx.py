@@ -1,0 +1,208 @@
+"""Matrix Market input and the binary CSR cache, on the CPU.
+
+spmvb_read_matrix_market must give the CSR the reference's own
+read_matrix_market gives (run from oracle/_ref) bit for bit, and the same
+error text, on files written here: every banner combination the reference
+accepts, comments and blank lines, CRLF line ends, repeated entries (kept,
+in the reference's order), symmetric mirrors, extra lines past the declared
+count, number forms, and every error it reports."""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+import spmvbench_b200 as S
+
+pytestmark = pytest.mark.skipif(not oracle.ref_available(), reason="oracle/_ref not built")
+
+
+def write(tmp_path, name, text):
+    p = tmp_path / name
+    p.write_bytes(text.encode())
+    return str(p)
+
+
+def same_as_reference(path, threads=0):
+    m, n, rp, ci, va = oracle.ref_read_matrix_market(path)
+    A = S.read_matrix_market(path, threads=threads)
+    assert (A.m, A.n) == (m, n)
+    np.testing.assert_array_equal(A.rowptr, rp)
+    np.testing.assert_array_equal(A.colind, ci)
+    assert A.values.tobytes() == va.tobytes()
+    return A
+
+
+def random_mtx(rng, rows, cols, entries, field="real", symmetry="general", dup_frac=0.1, comments=True,
+               crlf=False, fmt="{:.17g}"):
+    lines = [f"%%MatrixMarket matrix coordinate {field} {symmetry}"]
+    if comments:
+        lines += ["% written by the test", "%"]
+    lines.append(f"{rows} {cols} {entries}")
+    ii = rng.integers(1, rows + 1, entries)
+    jj = rng.integers(1, cols + 1, entries)
+    if symmetry == "symmetric":
+        ii, jj = np.maximum(ii, jj), np.minimum(ii, jj)
+    ndup = int(entries * dup_frac)
+    if ndup:
+        k = rng.integers(0, entries, ndup)
+        ii[-ndup:], jj[-ndup:] = ii[k], jj[k]
+    vals = rng.standard_normal(entries) * 10.0 ** rng.integers(-5, 5, entries)
+    for a, b, v in zip(ii, jj, vals):
+        if field == "pattern":
+            lines.append(f"{a} {b}")
+        elif field == "integer":
+            lines.append(f"{a} {b} {int(v * 1000)}")
+        else:
+            lines.append(f"{a} {b} {fmt.format(v)}")
+        if comments and rng.random() < 0.01:
+            lines.append("% interleaved comment")
+        if comments and rng.random() < 0.01:
+            lines.append("")
+    end = "\r\n" if crlf else "\n"
+    return end.join(lines) + end
+
+
+@pytest.mark.parametrize("field", ["real", "integer", "pattern"])
+@pytest.mark.parametrize("symmetry", ["general", "symmetric"])
+def test_matches_reference(tmp_path, field, symmetry):
+    rng = np.random.default_rng(hash((field, symmetry)) % 2**32)
+    p = write(tmp_path, "a.mtx", random_mtx(rng, 300, 300 if symmetry == "symmetric" else 250, 4000,
+                                            field, symmetry))
+    same_as_reference(p)
+
+
+def test_banner_case_crlf_and_number_forms(tmp_path):
+    text = ("%%matrixmarket MATRIX Coordinate REAL General\r\n%\r\n4 5 8\r\n"
+            "1 1 1\r\n1 2 -2.\r\n2 3 .5\r\n2 3 +7e2\r\n3 5 -1.25E-3\r\n4 4 3\r\n  4 1   0.1  \r\n"
+            "1 1 123456789012345678901234567890\r\n")
+    same_as_reference(write(tmp_path, "b.mtx", text))
+
+
+def test_repeated_entries_keep_the_reference_order(tmp_path):
+    # Rows long enough that std::sort does not fall back to insertion sort,
+    # with many repeated columns.
+    rng = np.random.default_rng(5)
+    lines = ["%%MatrixMarket matrix coordinate real general", "3 40 3000"]
+    for _ in range(3000):
+        lines.append(f"{rng.integers(1, 4)} {rng.integers(1, 41)} {rng.standard_normal():.17g}")
+    same_as_reference(write(tmp_path, "d.mtx", "\n".join(lines) + "\n"))
+
+
+def test_lines_past_the_declared_count_are_ignored(tmp_path):
+    text = ("%%MatrixMarket matrix coordinate real general\n3 3 2\n1 1 1\n2 2 2\n"
+            "3 3 3\nnot an entry\n9 9 9\n")
+    A = same_as_reference(write(tmp_path, "e.mtx", text))
+    assert A.nnz == 2
+
+
+def test_empty_matrices(tmp_path):
+    same_as_reference(write(tmp_path, "z1.mtx", "%%MatrixMarket matrix coordinate real general\n0 0 0\n"))
+    same_as_reference(write(tmp_path, "z2.mtx", "%%MatrixMarket matrix coordinate real general\n5 4 0\n"))
+
+
+def test_many_threads_give_the_same_csr(tmp_path):
+    rng = np.random.default_rng(9)
+    # Several MiB, so the entry lines are split over several threads, with
+    # symmetric mirrors and junk past the declared count at the end.
+    text = random_mtx(rng, 20000, 20000, 250000, "real", "symmetric", dup_frac=0.05)
+    text += "1 1 1\ngarbage line\n"
+    p = write(tmp_path, "big.mtx", text)
+    assert os.path.getsize(p) > 6 * 2**20
+    ref = same_as_reference(p, threads=1)
+    for t in (2, 3, 8, 0):
+        A = S.read_matrix_market(p, threads=t)
+        np.testing.assert_array_equal(A.rowptr, ref.rowptr)
+        np.testing.assert_array_equal(A.colind, ref.colind)
+        assert A.values.tobytes() == ref.values.tobytes()
+
+
+def test_an_error_past_the_declared_count_in_another_thread_is_ignored(tmp_path):
+    rng = np.random.default_rng(10)
+    body = random_mtx(rng, 1000, 1000, 200000, "real", "general", comments=False)
+    p = write(tmp_path, "tail.mtx", body + "1 1\n" * 50000 + "x y z\n")
+    for t in (1, 4, 16):
+        assert S.read_matrix_market(p, threads=t).nnz == 200000
+
+
+BAD = [
+    ("", "empty file"),
+    ("\n", "missing %%MatrixMarket banner"),
+    ("%%MatrixMarket vector coordinate real general\n1 1 1\n1 1 1\n", "only 'matrix' objects are supported"),
+    ("%%MatrixMarket matrix array real general\n1 1\n1\n", "only 'coordinate' format is supported"),
+    ("%%MatrixMarket matrix coordinate complex general\n1 1 1\n1 1 1 0\n", "complex matrices are not supported"),
+    ("%%MatrixMarket matrix coordinate double general\n1 1 1\n1 1 1\n", "unsupported field type"),
+    ("%%MatrixMarket matrix coordinate real skew-symmetric\n1 1 1\n1 1 1\n", "skew-symmetric"),
+    ("%%MatrixMarket matrix coordinate real hermitian\n1 1 1\n1 1 1\n", "unsupported symmetry"),
+    ("%%MatrixMarket matrix coordinate real\n1 1 1\n1 1 1\n", "unsupported symmetry"),
+    ("%%MatrixMarket matrix coordinate real general\n% only comments\n", "missing size line"),
+    ("%%MatrixMarket matrix coordinate real general\n3 x 3\n", "malformed size line"),
+    ("%%MatrixMarket matrix coordinate real general\n-1 3 0\n", "negative dimensions"),
+    ("%%MatrixMarket matrix coordinate real general\n3000000000 3 0\n", "dimensions exceed int32"),
+    ("%%MatrixMarket matrix coordinate real general\n3 3 1\n1\n", "malformed entry line"),
+    ("%%MatrixMarket matrix coordinate real general\n3 3 1\n1 2\n", "expected a value on entry line"),
+    ("%%MatrixMarket matrix coordinate real general\n3 3 1\n1 2 nan\n", "expected a value on entry line"),
+    ("%%MatrixMarket matrix coordinate real general\n3 3 1\n4 1 1\n", "index out of range"),
+    ("%%MatrixMarket matrix coordinate real general\n3 3 1\n0 1 1\n", "index out of range"),
+    ("%%MatrixMarket matrix coordinate real general\n3 3 1\n   \n", "malformed entry line"),
+    ("%%MatrixMarket matrix coordinate real general\n3 3 3\n1 1 1\n2 2 2\n", "expected 3 entries but found 2"),
+]
+
+
+@pytest.mark.parametrize("text,what", BAD, ids=[w for _, w in BAD])
+def test_errors_match_the_reference(tmp_path, text, what):
+    p = write(tmp_path, "bad.mtx", text)
+    with pytest.raises(RuntimeError) as ref_err:
+        oracle.ref_read_matrix_market(p)
+    with pytest.raises(S.SpmvbError) as err:
+        S.read_matrix_market(p)
+    assert err.value.status == 2
+    assert what in str(ref_err.value)
+    assert str(ref_err.value) in str(err.value)
+
+
+def test_missing_file(tmp_path):
+    p = str(tmp_path / "nope.mtx")
+    with pytest.raises(RuntimeError) as ref_err:
+        oracle.ref_read_matrix_market(p)
+    with pytest.raises(S.SpmvbError) as err:
+        S.read_matrix_market(p)
+    assert err.value.status == 9 and str(ref_err.value) in str(err.value)
+
+
+def test_csr_cache_round_trip(tmp_path):
+    A = S.generate(3, seed=3, scale_rows=20000)
+    p = str(tmp_path / "a.csrbin")
+    S.write_csr_cache(p, A)
+    assert os.path.getsize(p) == 40 + 4 * (A.m + 1) + 12 * A.nnz
+    B = S.read_csr_cache(p)
+    assert (B.m, B.n) == (A.m, A.n)
+    np.testing.assert_array_equal(B.rowptr, A.rowptr)
+    np.testing.assert_array_equal(B.colind, A.colind)
+    assert B.values.tobytes() == A.values.tobytes()
+
+
+def test_csr_cache_rejects_bad_files(tmp_path):
+    A = S.generate(1, seed=3, scale_rows=1000)
+    p = tmp_path / "a.csrbin"
+    S.write_csr_cache(str(p), A)
+    raw = bytearray(p.read_bytes())
+    (tmp_path / "trunc.csrbin").write_bytes(bytes(raw[:-8]))
+    bad_magic = bytes(b"X" + raw[1:])
+    (tmp_path / "magic.csrbin").write_bytes(bad_magic)
+    corrupt = bytearray(raw)
+    corrupt[40 + 4 * (A.m + 1)] = 0xFF  # first colind out of range
+    corrupt[40 + 4 * (A.m + 1) + 3] = 0x7F
+    (tmp_path / "corrupt.csrbin").write_bytes(bytes(corrupt))
+    for name in ("trunc", "magic", "corrupt"):
+        with pytest.raises(S.SpmvbError) as e:
+            S.read_csr_cache(str(tmp_path / f"{name}.csrbin"))
+        assert e.value.status == 2
+    with pytest.raises(S.SpmvbError) as e:
+        S.read_csr_cache(str(tmp_path / "missing.csrbin"))
+    assert e.value.status == 9
+    bad = S.CsrMatrix(2, 2, np.array([0, 2, 1], np.int32), np.array([0, 1], np.int32), np.ones(2))
+    with pytest.raises(S.SpmvbError):
+        S.write_csr_cache(str(tmp_path / "never.csrbin"), bad)
