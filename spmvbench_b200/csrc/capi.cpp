@@ -119,9 +119,9 @@ int64_t spmvb_matrix_st::device_bytes() const {
   int64_t b = rowptr.bytes() + colind.bytes() + values.bytes();
   b += ell_colind.bytes() + ell_values.bytes() + ell_rowlen.bytes();
   b += hyb_colind.bytes() + hyb_values.bytes() + hyb_rowlen.bytes() + hyb_long_rows.bytes() +
-       hyb_tail_ptr.bytes() + hyb_tail_colind.bytes() + hyb_tail_values.bytes() + hyb_chunk_row.bytes() +
-       hyb_first_split.bytes() + hyb_last_split.bytes() + hyb_split_rows.bytes() + hyb_split_count.bytes() +
-       hyb_empty_rows.bytes() + hyb_partial_first.bytes() + hyb_partial_last.bytes();
+       hyb_tail_ptr.bytes() + hyb_tail_colind.bytes() + hyb_tail_values.bytes() + hyb_chunk_start.bytes() +
+       hyb_chunk_row.bytes() + hyb_chunk_split.bytes() + hyb_split_rows.bytes() + hyb_split_first.bytes() +
+       hyb_split_count.bytes() + hyb_empty_rows.bytes() + hyb_partial.bytes();
   for (const auto* B : {&bcsr2, &bcsr4}) b += B->rowptr.bytes() + B->colind.bytes() + B->values.bytes();
   b += merge_tile_row.bytes() + merge_carry_row.bytes() + merge_carry_val.bytes();
   b += bucket_rows.bytes() + stage_in.bytes() + stage_out.bytes();

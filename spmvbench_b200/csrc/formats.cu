@@ -173,28 +173,33 @@ spmvb_status build_hyb(spmvb_matrix A, int forced_k) {
   const int n_long = static_cast<int>(long_rows.size());
   const int64_t slots = static_cast<int64_t>(A->m) * K;
   const int64_t tail = tail_ptr.back();
-  // Chunks of kHybChunk entries of the CSR part: the slot of the row holding
-  // each chunk's first entry; the rows spanning more than one chunk, and
-  // which of them each chunk holds first / last.
-  const int64_t n_chunks64 = (tail + kHybChunk - 1) / kHybChunk;
-  if (n_chunks64 > INT32_MAX / 2) return fail(SPMVB_ERR_UNSUPPORTED, "HYB: too many long-row entries");
-  const int n_chunks = static_cast<int>(n_chunks64);
-  std::vector<int32_t> chunk_row(static_cast<size_t>(n_chunks) + 1), split_rows;
-  std::vector<int32_t> first_split(std::max(n_chunks, 1), -1), last_split(std::max(n_chunks, 1), -1);
-  for (int c = 0, li = 0; c < n_chunks; ++c) {
-    const int64_t pos = static_cast<int64_t>(c) * kHybChunk;
-    while (tail_ptr[li + 1] <= pos) ++li;
-    chunk_row[c] = li;
+  // Chunks of the CSR part: whole rows packed greedily up to kHybChunk
+  // entries; a row longer than that cut into kHybChunk-entry segments.
+  std::vector<int64_t> chunk_start;
+  std::vector<int32_t> chunk_row, chunk_split, split_rows, split_first;
+  for (int li = 0; li < n_long;) {
+    const int64_t len = tail_ptr[li + 1] - tail_ptr[li];
+    if (len > kHybChunk) {
+      split_rows.push_back(li);
+      split_first.push_back(static_cast<int32_t>(chunk_start.size()));
+      for (int64_t o = 0; o < len; o += kHybChunk) {
+        chunk_start.push_back(tail_ptr[li] + o);
+        chunk_row.push_back(li);
+        chunk_split.push_back(static_cast<int32_t>(split_rows.size()) - 1);
+      }
+      ++li;
+      continue;
+    }
+    chunk_start.push_back(tail_ptr[li]);
+    chunk_row.push_back(li);
+    chunk_split.push_back(-1);
+    const int64_t start = tail_ptr[li];
+    while (li < n_long && tail_ptr[li + 1] - tail_ptr[li] <= kHybChunk && tail_ptr[li + 1] - start <= kHybChunk) ++li;
   }
-  chunk_row[n_chunks] = n_long;
-  for (int li = 0; li < n_long; ++li) {
-    const int64_t ca = tail_ptr[li] / kHybChunk, cb = (tail_ptr[li + 1] - 1) / kHybChunk;
-    if (ca == cb) continue;
-    const int si = static_cast<int>(split_rows.size());
-    split_rows.push_back(li);
-    last_split[ca] = si;
-    for (int64_t c = ca + 1; c <= cb; ++c) first_split[c] = si;
-  }
+  if (chunk_start.size() > static_cast<size_t>(INT32_MAX / 2)) return fail(SPMVB_ERR_UNSUPPORTED, "HYB: too many chunks");
+  const int n_chunks = static_cast<int>(chunk_start.size());
+  chunk_start.push_back(tail);
+  chunk_row.push_back(n_long);
 
   SPMVB_TRY(check_fits(A, static_cast<double>(slots + tail) * (4 + es) + 8.0 * A->m, "HYB"));
   SPMVB_TRY(A->hyb_colind.alloc(std::max<int64_t>(slots, 1) * 4));
@@ -204,14 +209,14 @@ spmvb_status build_hyb(spmvb_matrix A, int forced_k) {
   SPMVB_TRY(upload(A->hyb_tail_ptr, tail_ptr.data(), tail_ptr.size() * 8, tail_ptr.size() * 8));
   SPMVB_TRY(A->hyb_tail_colind.alloc((tail + kPad) * 4));
   SPMVB_TRY(A->hyb_tail_values.alloc((tail + kPad) * es));
+  SPMVB_TRY(upload(A->hyb_chunk_start, chunk_start.data(), chunk_start.size() * 8, chunk_start.size() * 8));
   SPMVB_TRY(upload(A->hyb_chunk_row, chunk_row.data(), chunk_row.size() * 4, chunk_row.size() * 4));
-  SPMVB_TRY(upload(A->hyb_first_split, first_split.data(), first_split.size() * 4, first_split.size() * 4));
-  SPMVB_TRY(upload(A->hyb_last_split, last_split.data(), last_split.size() * 4, last_split.size() * 4));
+  SPMVB_TRY(upload(A->hyb_chunk_split, chunk_split.data(), chunk_split.size() * 4, std::max<size_t>(chunk_split.size(), 1) * 4));
   SPMVB_TRY(upload(A->hyb_split_rows, split_rows.data(), split_rows.size() * 4, std::max<size_t>(split_rows.size(), 1) * 4));
+  SPMVB_TRY(upload(A->hyb_split_first, split_first.data(), split_first.size() * 4, std::max<size_t>(split_first.size(), 1) * 4));
   SPMVB_TRY(A->hyb_split_count.alloc(std::max<size_t>(split_rows.size(), 1) * 4));  // zero-filled
   SPMVB_TRY(upload(A->hyb_empty_rows, empty_rows.data(), empty_rows.size() * 4, std::max<size_t>(empty_rows.size(), 1) * 4));
-  SPMVB_TRY(A->hyb_partial_first.alloc(std::max<size_t>(n_chunks, 1) * 8));
-  SPMVB_TRY(A->hyb_partial_last.alloc(std::max<size_t>(n_chunks, 1) * 8));
+  SPMVB_TRY(A->hyb_partial.alloc(std::max<size_t>(n_chunks, 1) * 8));
   if (A->m > 0) {
     if (K > 0) {
       if (es == 8)

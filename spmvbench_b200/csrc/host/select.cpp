@@ -4,7 +4,8 @@
 // (src/select.cpp:93-165) unchanged, for callers that want its exact picks.
 //
 // spmvb_choose_spmv is the B200 rule set, ordered by what decides the cost
-// of each kernel: skewed rows need the merge path's equal share per thread,
+// of each kernel: skewed rows need an equal share of entries per warp (the
+// hybrid format's chunks),
 // mostly-dense 4x4 blocks let BCSR drop 15 of 16 column indices, nearly
 // uniform rows go to ELL (coalesced, all gathers in flight), long rows fill a
 // warp's vector loads, and the rest take the merge path.
@@ -113,11 +114,14 @@ extern "C" spmvb_status spmvb_choose_spmv(const spmvb_row_stats* sp, spmvb_choic
   if (!sp || !c) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null argument");
   const spmvb_row_stats& s = *sp;
   set(c, SPMVB_CSR_SCALAR, 1, 1, 1, -1, "");
-  // (0) Skewed row lengths: only the merge path keeps every thread busy.
+  // (0) Skewed row lengths: the hybrid format streams every row in equal
+  // chunks of entries (rows packed whole, long rows cut into segments), so
+  // every warp gets the same work; on the power-law 1M matrix it runs 1.47x
+  // faster than the merge path.
   if (s.cv_row_nnz > 1.5 || s.max_over_mean > 50.0) {
-    set(c, SPMVB_CSR_MERGE, 1, 1, 1, 0,
+    set(c, SPMVB_HYB, 1, 1, 1, 0,
         "cv=" + fmt(s.cv_row_nnz) + " or max/mean=" + fmt(s.max_over_mean) +
-            " indicates skew: merge-path gives every thread the same rows+nnz share");
+            " indicates skew: hybrid format, rows streamed in equal chunks of entries");
     return SPMVB_OK;
   }
   // (1) Mostly dense 4x4 blocks among the occupied ones: BCSR stores one

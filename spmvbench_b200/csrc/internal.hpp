@@ -136,8 +136,8 @@ struct spmvb_matrix_st {
   int hyb_n_split = 0;
   int hyb_n_empty = 0;
   spmvb::DevBuf hyb_colind, hyb_values, hyb_rowlen, hyb_long_rows, hyb_tail_ptr,
-      hyb_tail_colind, hyb_tail_values, hyb_chunk_row, hyb_first_split, hyb_last_split,
-      hyb_split_rows, hyb_split_count, hyb_empty_rows, hyb_partial_first, hyb_partial_last;
+      hyb_tail_colind, hyb_tail_values, hyb_chunk_start, hyb_chunk_row, hyb_chunk_split, hyb_split_rows,
+      hyb_split_first, hyb_split_count, hyb_empty_rows, hyb_partial;
 
   // BCSR 2x2 and 4x4
   struct Bcsr {

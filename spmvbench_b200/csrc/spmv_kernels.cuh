@@ -441,37 +441,20 @@ __global__ void __launch_bounds__(256)
 //
 // ELL blocks: one thread per row with len <= K, csr_omp order (bit-identical).
 //
-// Chunk blocks: the long rows are streamed in chunks of kHybChunk entries, one
-// warp per chunk, so every warp gets the same number of entries whatever the
-// row lengths. Lane l loads entries l, l+32, ... of its chunk (coalesced),
-// every gather of the chunk is in flight before any product is formed. A
-// chunk inside one row is reduced by the warp in a fixed order (lane partials
-// over p = l + 32i, then a butterfly); otherwise the products go to the warp's
-// slice of shared memory and lane l sums the pieces of rows li0+l, li0+l+32,
-// ... left to right. A row wholly inside the chunk is written to y; a piece
-// of a split row goes to partial_last / partial_first, and the warp whose
-// piece completes a split row (per-row counter) adds its pieces in a fixed
-// order: partial_last of its first chunk, then the partial_first of the later
-// ones (lane partials, butterfly). Deterministic; long rows are re-associated
-// (bounded by 2*gamma_n*sum|a_ij x_j|).
+// Chunk blocks, one warp per chunk of at most kHybChunk entries: lane l loads
+// entries l, l+32, ... (coalesced) and every gather of the chunk is in flight
+// before any product is formed.
+//  - Packed chunk (whole rows): the products go to the warp's slice of shared
+//    memory and lane l adds rows chunk_row[c]+l, +l+32, ... left to right from
+//    zero, the csr_omp order, so these rows are bit-identical too. The lane's
+//    first row's bounds and id are loaded with the chunk's entries.
+//  - Segment of a row longer than kHybChunk: the warp reduces it in a fixed
+//    order (lane partials over p = l + 32i, then a butterfly) into partial[c];
+//    the warp whose partial completes the row (per-row counter) adds the
+//    row's partials in chunk order (lane partials, butterfly) and writes y.
+//    Deterministic, re-associated (bounded by 2*gamma_n*sum|a_ij x_j|).
 //
 // Remaining blocks: y = 0 for the empty rows when K = 0.
-template <typename Acc>
-__device__ __forceinline__ void hyb_finish_split(const HybView& H, int si, Acc* __restrict__ y, int lane) {
-  const int li = H.split_rows[si];
-  const int ca = static_cast<int>(H.tail_ptr[li] / kHybChunk);
-  const int cb = static_cast<int>((H.tail_ptr[li + 1] - 1) / kHybChunk);
-  const Acc* pf = static_cast<const Acc*>(H.partial_first);
-  const Acc* pl = static_cast<const Acc*>(H.partial_last);
-  Acc v = Acc(0);
-  for (int c = ca + 1 + lane; c <= cb; c += kWarp) v = add_rn(v, __ldcg(pf + c));
-  v = group_sum<kWarp>(v);
-  if (lane == 0) {
-    y[H.long_rows[li]] = add_rn(__ldcg(pl + ca), v);
-    H.split_count[si] = 0;  // ready for the next launch
-  }
-}
-
 template <typename T, typename Acc>
 __global__ void __launch_bounds__(256)
     hyb_rows(HybView H, const T* __restrict__ x, Acc* __restrict__ y) {
@@ -499,85 +482,78 @@ __global__ void __launch_bounds__(256)
   const int c = cb_index * W + wib;
   if (c >= H.n_chunks) return;
   const T* __restrict__ tv = static_cast<const T*>(H.tail_values);
-  const int64_t c0 = static_cast<int64_t>(c) * kHybChunk;
-  const int64_t c1 = min(c0 + kHybChunk, H.tail_nnz);
+  const int64_t e0 = H.chunk_start[c];
+  const int span = static_cast<int>(H.chunk_start[c + 1] - e0);
   const int li0 = H.chunk_row[c];
-  const int nxt = H.chunk_row[c + 1];
-  const int li1 = (H.tail_ptr[nxt] == c1) ? nxt - 1 : nxt;  // row holding entry c1 - 1
-  Acc* __restrict__ pf = static_cast<Acc*>(H.partial_first);
-  Acc* __restrict__ pl = static_cast<Acc*>(H.partial_last);
+  const int li_end = H.chunk_row[c + 1];  // packed: rows li0 .. li_end-1
 
   int col[PER];
   T val[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
-    const int64_t p = c0 + lane + i * kWarp;
-    col[i] = p < c1 ? ld_stream(H.tail_colind + p, ps) : 0;
-    val[i] = p < c1 ? ld_stream(tv + p, ps) : T(0);
+    const int q = lane + i * kWarp;
+    col[i] = q < span ? ld_stream(H.tail_colind + e0 + q, ps) : 0;
+    val[i] = q < span ? ld_stream(tv + e0 + q, ps) : T(0);
+  }
+  const int64_t rs0 = H.tail_ptr[li0];
+  const int64_t re0 = H.tail_ptr[li0 + 1];
+  // The lane's first row (packed chunks), loaded alongside the entries.
+  const int my = li0 + lane;
+  int64_t my_s = 0, my_e = 0;
+  int my_row = 0;
+  if (my < li_end) {
+    my_s = H.tail_ptr[my];
+    my_e = H.tail_ptr[my + 1];
+    my_row = H.long_rows[my];
   }
   Acc pr[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i)
-    pr[i] = (c0 + lane + i * kWarp < c1) ? prod<Acc>(val[i], ld_keep(x + col[i], pk)) : Acc(0);
+    pr[i] = (lane + i * kWarp < span) ? prod<Acc>(val[i], ld_keep(x + col[i], pk)) : Acc(0);
 
-  // A lane can complete at most two split rows: the chunk's first row
-  // (through partial_first) and its last row (through partial_last).
-  int fin_first = -1, fin_last = -1;
-  auto completes = [&](int si) -> bool {
-    __threadfence();  // the partial is visible before the count
-    const int li = H.split_rows[si];
-    const int pieces = static_cast<int>((H.tail_ptr[li + 1] - 1) / kHybChunk - H.tail_ptr[li] / kHybChunk) + 1;
-    return atomicAdd(H.split_count + si, 1) == pieces - 1;
-  };
-  if (li0 == li1) {
+  if (re0 - rs0 > kHybChunk) {
+    // Segment of a cut row.
     Acc v = Acc(0);
 #pragma unroll
-    for (int i = 0; i < PER; ++i) v = add_rn(v, pr[i]);  // entries past c1 add exact zeros
+    for (int i = 0; i < PER; ++i) v = add_rn(v, pr[i]);  // entries past the span add exact zeros
     v = group_sum<kWarp>(v);
+    Acc* part = static_cast<Acc*>(H.partial);
+    const int si = H.chunk_split[c];
+    const int first = H.split_first[si];
+    const int pieces = static_cast<int>((re0 - rs0 + kHybChunk - 1) / kHybChunk);
+    int last = 0;
     if (lane == 0) {
-      const int64_t rs = H.tail_ptr[li0], re = H.tail_ptr[li0 + 1];
-      if (rs < c0) {
-        pf[c] = v;
-        if (completes(H.first_split[c])) fin_first = H.first_split[c];
-      } else if (re > c1) {
-        pl[c] = v;
-        if (completes(H.last_split[c])) fin_last = H.last_split[c];
-      } else {
-        y[H.long_rows[li0]] = v;
-      }
+      part[c] = v;
+      __threadfence();  // the partial is visible before the count
+      last = atomicAdd(H.split_count + si, 1) == pieces - 1;
     }
-  } else {
-#pragma unroll
-    for (int i = 0; i < PER; ++i) s_prod[wib][lane + i * kWarp] = pr[i];
-    __syncwarp();
-    for (int li = li0 + lane; li <= li1; li += kWarp) {
-      const int64_t rs = H.tail_ptr[li], re = H.tail_ptr[li + 1];
-      const int a = static_cast<int>(max(rs, c0) - c0);
-      const int b = static_cast<int>(min(re, c1) - c0);
-      Acc v = Acc(0);
-      for (int q = a; q < b; ++q) v = add_rn(v, s_prod[wib][q]);
-      if (rs < c0) {
-        pf[c] = v;
-        if (completes(H.first_split[c])) fin_first = H.first_split[c];
-      } else if (re > c1) {
-        pl[c] = v;
-        if (completes(H.last_split[c])) fin_last = H.last_split[c];
-      } else {
-        y[H.long_rows[li]] = v;
-      }
-    }
-  }
-  // The warp finishes the split rows whose last piece it wrote.
-  for (int k = 0; k < 2; ++k) {
-    const int mine = k == 0 ? fin_first : fin_last;
-    unsigned todo = __ballot_sync(0xffffffffu, mine >= 0);
-    while (todo) {
-      const int src = __ffs(todo) - 1;
-      todo &= todo - 1;
-      const int si = __shfl_sync(0xffffffffu, mine, src);
+    if (__shfl_sync(0xffffffffu, last, 0)) {
       __threadfence();
-      hyb_finish_split<Acc>(H, si, y, lane);
+      Acc t = Acc(0);
+      for (int k = lane; k < pieces; k += kWarp) t = add_rn(t, __ldcg(part + first + k));
+      t = group_sum<kWarp>(t);
+      if (lane == 0) {
+        y[H.long_rows[li0]] = t;
+        H.split_count[si] = 0;  // ready for the next launch
+      }
     }
+    return;
+  }
+  // Packed chunk: whole rows.
+#pragma unroll
+  for (int i = 0; i < PER; ++i) s_prod[wib][lane + i * kWarp] = pr[i];
+  __syncwarp();
+  for (int li = my; li < li_end; li += kWarp) {
+    if (li != my) {
+      my_s = H.tail_ptr[li];
+      my_e = H.tail_ptr[li + 1];
+      my_row = H.long_rows[li];
+    }
+    const int a = static_cast<int>(my_s - e0);
+    const int b = static_cast<int>(my_e - e0);
+    Acc v = Acc(0);
+    for (int q = a; q < b; ++q) v = add_rn(v, s_prod[wib][q]);
+    y[my_row] = v;
   }
 }
 

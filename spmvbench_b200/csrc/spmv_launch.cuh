@@ -101,14 +101,14 @@ spmvb_status launch_spmv(spmvb_matrix A, spmvb_kernel kernel, int lanes,
       h.tail_ptr = A->hyb_tail_ptr.as<int64_t>();
       h.tail_colind = A->hyb_tail_colind.as<int>();
       h.tail_values = A->hyb_tail_values.get();
+      h.chunk_start = A->hyb_chunk_start.as<int64_t>();
       h.chunk_row = A->hyb_chunk_row.as<int>();
-      h.first_split = A->hyb_first_split.as<int>();
-      h.last_split = A->hyb_last_split.as<int>();
+      h.chunk_split = A->hyb_chunk_split.as<int>();
       h.split_rows = A->hyb_split_rows.as<int>();
+      h.split_first = A->hyb_split_first.as<int>();
       h.split_count = A->hyb_split_count.as<int>();
       h.empty_rows = A->hyb_empty_rows.as<int>();
-      h.partial_first = A->hyb_partial_first.get();
-      h.partial_last = A->hyb_partial_last.get();
+      h.partial = A->hyb_partial.get();
       h.tail_nnz = A->hyb_tail_nnz;
       h.n_long = A->hyb_n_long;
       h.n_chunks = A->hyb_n_chunks;

@@ -38,16 +38,17 @@ struct EllView {
 // Hybrid ELL(K) + CSR. Rows with len <= K keep their entries in the
 // column-major ELL part (row_lengths = len); rows longer than K ("long rows",
 // row_lengths = -1) are stored whole, back to back, in a CSR part indexed by
-// long-row slot, streamed in equal chunks of kHybChunk entries. chunk_row[c]
-// is the slot of the row holding entry c*kHybChunk (chunk_row[n_chunks] =
-// n_long). Rows spanning more than one chunk ("split rows", slots in
-// split_rows) leave one partial per chunk: partial_last[c] for the chunk
-// where the row starts, partial_first[c] for every later chunk it reaches;
-// first_split[c] / last_split[c] name the split row whose piece chunk c
-// holds first / last (-1: none), and split_count[s] counts the pieces
-// written (0 between launches). With K = 0 the empty rows are listed in
-// empty_rows. One launch: ell_blocks blocks of ELL rows, chunk_blocks blocks
-// of chunks, then the empty rows.
+// long-row slot. The CSR part is cut into chunks of at most kHybChunk
+// entries: a "packed" chunk holds whole rows (consecutive slots
+// chunk_row[c] .. chunk_row[c+1]-1); a row longer than kHybChunk is cut into
+// "segment" chunks of kHybChunk entries (its last one shorter), one per
+// chunk. chunk_start[c] is the chunk's first entry (chunk_start[n_chunks] =
+// tail_nnz). Segments leave a partial each (partial[c]); chunk_split[c] names
+// the cut row's index s among split_rows (-1 for packed chunks), split_first
+// [s] its first chunk, split_count[s] counts the partials written (0 between
+// launches). With K = 0 the empty rows are listed in empty_rows. One launch:
+// ell_blocks blocks of ELL rows, chunk_blocks blocks of chunks, then the
+// empty rows.
 constexpr int kHybChunk = 256;
 
 struct HybView {
@@ -56,14 +57,14 @@ struct HybView {
   const int64_t* tail_ptr = nullptr;  // n_long + 1 offsets into the CSR part
   const int* tail_colind = nullptr;   // + kPad
   const void* tail_values = nullptr;
-  const int* chunk_row = nullptr;     // n_chunks + 1
-  const int* first_split = nullptr;   // n_chunks
-  const int* last_split = nullptr;    // n_chunks
-  const int* split_rows = nullptr;    // n_split
-  int* split_count = nullptr;         // n_split
-  const int* empty_rows = nullptr;    // n_empty (K = 0 only)
-  void* partial_first = nullptr;      // n_chunks
-  void* partial_last = nullptr;       // n_chunks
+  const int64_t* chunk_start = nullptr;  // n_chunks + 1
+  const int* chunk_row = nullptr;        // n_chunks + 1
+  const int* chunk_split = nullptr;      // n_chunks
+  const int* split_rows = nullptr;       // n_split
+  const int* split_first = nullptr;      // n_split
+  int* split_count = nullptr;            // n_split
+  const int* empty_rows = nullptr;       // n_empty (K = 0 only)
+  void* partial = nullptr;               // n_chunks, of the accumulator type
   int64_t tail_nnz = 0;
   int n_long = 0;
   int n_chunks = 0;

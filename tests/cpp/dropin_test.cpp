@@ -91,7 +91,7 @@ static void cpu_tests() {
   EXPECT(c.kernel == KernelId::CsrVector && c.lanes == 16 && !c.reason.empty());
   t.cv_row_nnz = 5.0;
   t.max_over_mean = 200.0;
-  EXPECT(choose_spmv(t).kernel == KernelId::CsrMerge);
+  EXPECT(choose_spmv(t).kernel == KernelId::Hyb);
   EXPECT(std::string(kernel_name(KernelId::Hyb)) == "hyb");
 }
 

@@ -130,7 +130,7 @@ def test_choose_reference_rules_match_oracle_grid():
 
 
 def test_choose_b200_rules():
-    assert S.choose_spmv(dict(nnz=10 ** 7, mean_row_nnz=5, cv_row_nnz=30, max_over_mean=9000))["name"] == "csr_merge"
+    assert S.choose_spmv(dict(nnz=10 ** 7, mean_row_nnz=5, cv_row_nnz=30, max_over_mean=9000))["name"] == "hyb"
     assert S.choose_spmv(dict(nnz=10 ** 7, mean_row_nnz=32, cv_row_nnz=0,
                               dense_share_of_stored_4x4=1.0))["name"] == "bcsr"
     assert S.choose_spmv(dict(nnz=10 ** 7, mean_row_nnz=16, cv_row_nnz=0, ell_padding_overhead=1.0))["name"] == "ell"
