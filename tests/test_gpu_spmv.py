@@ -15,7 +15,8 @@ pytestmark = pytest.mark.gpu
 
 # (kernel, lanes, block, how it must match csr_omp): "exact" = bit for bit,
 # "bcsr" = bit for bit against spmv_bcsr_cpu and bounded against csr_omp,
-# "hyb" = bit for bit on rows held in the ELL part, bounded on long rows.
+# "hyb" = bit for bit on rows up to max(K, 256) entries, bounded on the rows
+# cut into segments.
 VARIANTS = [(S.CSR_SCALAR, 1, 4, "exact")] + \
            [(S.CSR_VECTOR, L, 4, "bound") for L in (2, 4, 8, 16, 32)] + \
            [(S.CSR_WARP, 1, 4, "bound"), (S.CSR_MERGE, 1, 4, "bound"), (S.ELL, 1, 4, "exact"),
@@ -46,9 +47,11 @@ def check_variant(ctx, A, x, dtype, acc, kernel, lanes, block, how, label, M=Non
         if np.unique(keys).size == keys.size:
             assert_rows_within_bound(A, x, ref, got, dtype, acc, tag)
     elif how == "hyb":
+        # rows in the ELL part (len <= K) and rows packed whole into a chunk
+        # (len <= 256) are summed left to right from zero: bit for bit
         K = M.info()["hyb_width"]
-        short = np.diff(A.rowptr) <= K
-        assert_bitwise(ref[short], got[short], tag + " (ELL rows)")
+        short = np.diff(A.rowptr) <= max(K, 256)
+        assert_bitwise(ref[short], got[short], tag + " (whole rows)")
         assert_rows_within_bound(A, x, ref, got, dtype, acc, tag)
     else:
         assert_rows_within_bound(A, x, ref, got, dtype, acc, tag)
@@ -194,9 +197,9 @@ def test_host_buffer_entry_point_matches_device(ctx):
 @pytest.mark.parametrize("K", [-1, 1, 3, 8, 64, 257])
 def test_hyb_widths_are_exact_bounded_and_deterministic(ctx, K):
     """Every width of the hybrid format (-1 = width 0: every row chunked):
-    rows up to K bit-identical to csr_omp, long rows (chunked, some split
-    across chunks) within the gamma_n bound, and the same bits on every
-    rerun (the split rows' counters reset themselves)."""
+    rows up to max(K, 256) bit-identical to csr_omp, rows cut into segments
+    within the gamma_n bound, and the same bits on every rerun (the cut rows'
+    counters reset themselves)."""
     A = S.generate(3, seed=57, scale_rows=150000)
     x = S.generate_vector(58, A.n)
     M = S.DeviceMatrix(ctx, A, S.F64)
