@@ -21,8 +21,11 @@ Extra objects on the same line:
   cpu_baseline  the reference's own csr_omp (oracle/_ref, compiled from the
                 reference sources; the C restatement if that is absent) on
                 the same matrix, all host threads, rank 0 at N=1
-  e2e           the same metric through spmvb_spmv_host (pinned host x in,
-                host y out, copies inside the timed region)
+  e2e           the same metric through the host-buffer API: pinned host x
+                copied in and y copied out every step, inside the timed
+                region; the streamed pipeline (spmvb_pipeline_submit, calls
+                overlapped) is the value, spmvb_spmv_host's synchronous call
+                is reported beside it
   spmm_k64      fp64 SpMM Y = A X, X 1,000,000 x 64, same matrix, per-rank
   iterated      x <- A x on ONE uniform matrix row-sharded over the N ranks
                 (nnz-balanced), x slices exchanged each step by ncclAllGather
@@ -327,23 +330,49 @@ def main():
     # per entry from the L2-resident x), measured live on this GPU.
     gather_peak = ctx.gather_rate(A.n, A.nnz)
     gathers_achieved = A.nnz / (ms * 1e-3)
-    # ---- e2e through the host-buffer entry point ----
+    # ---- e2e through the host-buffer entry points ----
+    # Per step: copy x (pinned host) in, SpMV, copy y out to pinned host.
+    # Headline: the streamed pipeline (3 calls in flight, so one call's copy
+    # in overlaps another's copy out and a third's kernel); beside it the
+    # synchronous spmvb_spmv_host call.
     xp = torch.from_numpy(xh.copy()).pin_memory()
-    yp = torch.empty(A.m, dtype=torch.float64).pin_memory()
-    xp_np, yp_np = xp.numpy(), yp.numpy()
+    yps = [torch.empty(A.m, dtype=torch.float64).pin_memory() for _ in range(3)]
+    xp_np = xp.numpy()
     for _ in range(3):
-        M.spmv_host(xp_np, kernel=kernel, lanes=lanes, block=block, out=yp_np, stream=stream)
+        M.spmv_host(xp_np, kernel=kernel, lanes=lanes, block=block, out=yps[0].numpy(), stream=stream)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        M.spmv_host(xp_np, kernel=kernel, lanes=lanes, block=block, out=yp_np, stream=stream)
+        M.spmv_host(xp_np, kernel=kernel, lanes=lanes, block=block, out=yps[0].numpy(), stream=stream)
     e1.record(stream)
     e1.synchronize()
     barrier()
+    sync_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    pipe = S.Pipeline(M, depth=3)
+    for i in range(3):
+        pipe.submit(xp_np, yps[i].numpy(), kernel=kernel, lanes=lanes, block=block)
+    pipe.wait()
+    barrier()
+    launches_pipe0 = S.launch_count()
+    e0.record(stream)
+    pipe.fork(stream)
+    for i in range(args.steps):
+        pipe.submit(xp_np, yps[i % 3].numpy(), kernel=kernel, lanes=lanes, block=block)
+    pipe.join(stream)
+    e1.record(stream)
+    e1.synchronize()
+    pipe.wait()
+    barrier()
+    launches_pipe = S.launch_count() - launches_pipe0
+    pipe.close()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
     e2e = {"value": world * 2.0 * A.nnz / (e2e_ms * 1e-3) / 1e9, "unit": "GFLOP/s",
-           "ms_per_step": e2e_ms, "h2d_bytes_per_step": int(A.n * 8), "d2h_bytes_per_step": int(A.m * 8)}
+           "ms_per_step": e2e_ms, "h2d_bytes_per_step": int(A.n * 8), "d2h_bytes_per_step": int(A.m * 8),
+           "api": "spmvb_pipeline_submit, 3 calls in flight, pinned host x in and y out every step",
+           "kernel_launches": int(launches_pipe),
+           "sync_call": {"value": world * 2.0 * A.nnz / (sync_ms * 1e-3) / 1e9, "ms_per_step": sync_ms,
+                         "api": "spmvb_spmv_host"}}
 
     # ---- SpMM k=64 on the same matrix ----
     k = 64

@@ -288,6 +288,31 @@ spmvb_status spmvb_generate(int which, uint64_t seed, int32_t scale_rows,
 /* x_i ~ U(-1,1) from a seeded 64-bit generator, shared by oracle and GPU. */
 spmvb_status spmvb_generate_vector(uint64_t seed, int64_t len, double* h_out);
 
+/* ---- streamed SpMV over host buffers ------------------------------------------- */
+/* No reference counterpart (SpmvRunner copies x in, runs and copies y out
+ * synchronously, src/cuda/spmv_cuda.cu:292-330,476-498). A pipeline keeps
+ * up to `depth` (1..16) host-buffer SpMVs in flight, each on its own stream
+ * and device staging, so with pinned host buffers one call's copy of x in,
+ * another's kernel and a third's copy of y out overlap. */
+typedef struct spmvb_pipeline_st* spmvb_pipeline;
+spmvb_status spmvb_pipeline_create(spmvb_matrix A, int depth,
+                                   spmvb_pipeline* out);
+/* Later submissions start after the work already enqueued on `stream`. */
+spmvb_status spmvb_pipeline_fork(spmvb_pipeline P, void* stream);
+/* Enqueues y = A x (host x: n entries, host y: m entries of `acc`) on the
+ * next slot and returns. h_x must stay unchanged and h_y must not be read
+ * until the call is waited for (spmvb_pipeline_wait, or work joined onto a
+ * stream); a slot's staging is reused only after its previous call ends. */
+spmvb_status spmvb_pipeline_submit(spmvb_pipeline P, spmvb_kernel kernel,
+                                   int lanes, int block, const void* h_x,
+                                   void* h_y, spmvb_dtype acc);
+/* `stream` waits for every call submitted so far. */
+spmvb_status spmvb_pipeline_join(spmvb_pipeline P, void* stream);
+/* Waits for every call submitted so far; reports a kernel's bounded-wait
+ * failure like the other host entry points. */
+spmvb_status spmvb_pipeline_wait(spmvb_pipeline P);
+spmvb_status spmvb_pipeline_destroy(spmvb_pipeline P);
+
 /* ---- input formats ------------------------------------------------------------- */
 /* Host CSR read from a file (f64 values; a caller wanting f32 converts with
  * round-to-nearest, as the reference's static_cast<float> does). */

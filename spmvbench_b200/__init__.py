@@ -21,7 +21,7 @@ from ._lib import (BCSR, CSR_MERGE, CSR_SCALAR, CSR_VECTOR, CSR_WARP, ELL, F32, 
 
 __all__ = [
     "CsrMatrix", "Context", "DeviceMatrix", "DistMatrix", "SpmvbError", "generate",
-    "read_matrix_market", "write_csr_cache", "read_csr_cache",
+    "read_matrix_market", "write_csr_cache", "read_csr_cache", "Pipeline",
     "generate_vector", "row_stats", "choose_spmv", "choose_spmv_reference", "partition_rows",
     "launch_count", "gpu_available", "csr_validate", "shard_csr", "query_gpu", "kernel_name", "nccl_unique_id",
     "CSR_SCALAR", "CSR_VECTOR", "CSR_WARP", "CSR_MERGE", "ELL", "BCSR", "HYB", "F32", "F64",
@@ -346,6 +346,46 @@ class DeviceMatrix:
         va = np.zeros(max(bnnz, 1) * block * block, _np_dtype(self.dtype))
         call("spmvb_matrix_export_bcsr", self.handle, block, _ptr(rp), _ptr(ci), _ptr(va))
         return rp, ci[:bnnz], va[:bnnz * block * block]
+
+
+class Pipeline:
+    """Streamed y = A x over host buffers: up to `depth` calls in flight on
+    their own streams (pinned host buffers let copies in, kernels and copies
+    out of different calls overlap). Keep x unchanged and y unread until
+    wait() (or join())."""
+
+    def __init__(self, M: "DeviceMatrix", depth: int = 3):
+        h = C.c_void_p()
+        call("spmvb_pipeline_create", M.handle, depth, C.byref(h))
+        self.handle = h
+        self.M = M
+        self._keep = []
+
+    def fork(self, stream):
+        call("spmvb_pipeline_fork", self.handle, _stream_ptr(stream))
+
+    def submit(self, x: np.ndarray, y: np.ndarray, kernel: int = CSR_SCALAR, lanes: int = 4, block: int = 4,
+               acc: int | None = None):
+        acc = self.M.dtype if acc is None else acc
+        assert x.dtype == _np_dtype(self.M.dtype) and x.flags.c_contiguous and x.size >= self.M.n
+        assert y.dtype == _np_dtype(acc) and y.flags.c_contiguous and y.size >= self.M.m
+        self._keep.append((x, y))  # alive until wait()
+        call("spmvb_pipeline_submit", self.handle, kernel, lanes, block, _ptr(x), _ptr(y), acc)
+
+    def join(self, stream):
+        call("spmvb_pipeline_join", self.handle, _stream_ptr(stream))
+
+    def wait(self):
+        call("spmvb_pipeline_wait", self.handle)
+        self._keep.clear()
+
+    def close(self):
+        if getattr(self, "handle", None):
+            load().spmvb_pipeline_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.close()
 
 
 class DistMatrix:

@@ -117,6 +117,12 @@ SIGNATURES = {
     "spmvb_dist_enable_peer": (C.c_int, [P, P]),
     "spmvb_dist_exchange": (C.c_int, [P]),
     "spmvb_dist_get_info": (C.c_int, [P, I32P, I32P, I32P, I64P]),
+    "spmvb_pipeline_create": (C.c_int, [P, C.c_int, C.POINTER(P)]),
+    "spmvb_pipeline_fork": (C.c_int, [P, P]),
+    "spmvb_pipeline_submit": (C.c_int, [P, C.c_int, C.c_int, C.c_int, P, P, C.c_int]),
+    "spmvb_pipeline_join": (C.c_int, [P, P]),
+    "spmvb_pipeline_wait": (C.c_int, [P]),
+    "spmvb_pipeline_destroy": (C.c_int, [P]),
     "spmvb_read_matrix_market": (C.c_int, [C.c_char_p, C.c_int, C.POINTER(P)]),
     "spmvb_csr_cache_write": (C.c_int, [C.c_char_p, C.c_int32, C.c_int32, C.c_int64, P, P, P]),
     "spmvb_csr_cache_read": (C.c_int, [C.c_char_p, C.POINTER(P)]),

@@ -107,6 +107,28 @@ def test_single_rank_iteration_matches_oracle(ctx):
     D.close()
 
 
+@pytest.mark.parametrize("depth", [1, 3])
+def test_pipeline_streams_host_buffers(ctx, depth):
+    """Streamed host-buffer SpMV: 7 calls with different x and separate y
+    buffers (pinned), several in flight, each equal to csr_omp bit for bit;
+    fork/join order them against a caller's stream."""
+    A = S.generate(2, seed=82, scale_rows=80000)
+    M = S.DeviceMatrix(ctx, A, S.F64)
+    P = S.Pipeline(M, depth=depth)
+    xs = [torch.from_numpy(S.generate_vector(83 + i, A.n)).pin_memory() for i in range(7)]
+    ys = [torch.full((A.m,), float("nan"), dtype=torch.float64).pin_memory() for _ in range(7)]
+    s = torch.cuda.Stream()
+    P.fork(s)
+    for i in range(7):
+        P.submit(xs[i].numpy(), ys[i].numpy(), kernel=S.ELL if i % 2 else S.CSR_SCALAR)
+    P.join(s)
+    s.synchronize()
+    P.wait()
+    for i in range(7):
+        assert_bitwise(oracle_y(A, xs[i].numpy(), S.F64, S.F64), ys[i].numpy(), f"pipeline call {i}")
+    P.close()
+
+
 @pytest.mark.parametrize("kernel", ["ELL", "CSR_MERGE", "CSR_SCALAR"])
 def test_single_rank_peer_exchange(ctx, kernel):
     """Peer exchange with one rank: the SpMV writes the next x itself (fused
