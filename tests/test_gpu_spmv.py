@@ -234,3 +234,31 @@ def test_hyb_width_zero_writes_empty_rows(ctx, dtype, acc):
     y = run_spmv(M, x, S.HYB, acc=acc)
     assert np.all(y[::7] == 0.0)
     assert_rows_within_bound(A, x, oracle_y(A, x, dtype, acc), y, dtype, acc, "hyb K=0")
+
+
+@pytest.mark.parametrize("dtype,acc", DTYPE_PAIRS)
+def test_bcsr_long_block_rows_and_empty_chunks(ctx, dtype, acc):
+    """BCSR on the shapes the streamed kernel's chunk plan has to handle: a
+    block row longer than one chunk (the plain kernel takes that matrix),
+    and long runs of empty block rows (chunks whose copy has no bytes);
+    both bit for bit against spmv_bcsr_cpu."""
+    rng = np.random.default_rng(61)
+    m = n = 4000
+    lens = np.zeros(m, np.int64)
+    lens[1000:1100] = rng.integers(1, 30, 100)   # rows 0..999 and 1100.. mostly empty
+    lens[3000:3050] = rng.integers(1, 30, 50)
+    cols = [np.sort(rng.choice(n, int(k), replace=False)) for k in lens]
+    dense = np.sort(rng.choice(n, 3000, replace=False))  # one long row: > 64 4x4 blocks
+    for label, heavy in (("empty runs", False), ("long block row", True)):
+        rl = lens.copy()
+        cl = list(cols)
+        if heavy:
+            rl[2000] = dense.size
+            cl[2000] = dense
+        rowptr = np.concatenate([[0], np.cumsum(rl)]).astype(np.int32)
+        colind = np.concatenate(cl).astype(np.int32)
+        A = S.CsrMatrix(m, n, rowptr, colind, rng.uniform(-1, 1, colind.size))
+        x = mixed_x(n)
+        M = S.DeviceMatrix(ctx, A, dtype)
+        for block in (2, 4):
+            check_variant(ctx, A, x, dtype, acc, S.BCSR, 1, block, "bcsr", label, M)
