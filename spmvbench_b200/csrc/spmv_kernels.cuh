@@ -460,7 +460,7 @@ __global__ void __launch_bounds__(256)
     hyb_rows(HybView H, const T* __restrict__ x, Acc* __restrict__ y) {
   constexpr int W = 256 / kWarp;
   constexpr int PER = kHybChunk / kWarp;
-  __shared__ Acc s_prod[W][kHybChunk];
+  __shared__ Acc s_prod[W][swz_size<Acc>(kHybChunk)];  // padded: conflict-free row sums
   const uint64_t ps = policy_evict_first();
   const uint64_t pk = policy_evict_last();
   if (static_cast<int>(blockIdx.x) < H.ell_blocks) {
@@ -541,7 +541,7 @@ __global__ void __launch_bounds__(256)
   }
   // Packed chunk: whole rows.
 #pragma unroll
-  for (int i = 0; i < PER; ++i) s_prod[wib][lane + i * kWarp] = pr[i];
+  for (int i = 0; i < PER; ++i) s_prod[wib][swz<Acc>(lane + i * kWarp)] = pr[i];
   __syncwarp();
   for (int li = my; li < li_end; li += kWarp) {
     if (li != my) {
@@ -552,7 +552,7 @@ __global__ void __launch_bounds__(256)
     const int a = static_cast<int>(my_s - e0);
     const int b = static_cast<int>(my_e - e0);
     Acc v = Acc(0);
-    for (int q = a; q < b; ++q) v = add_rn(v, s_prod[wib][q]);
+    for (int q = a; q < b; ++q) v = add_rn(v, s_prod[wib][swz<Acc>(q)]);
     y[my_row] = v;
   }
 }
