@@ -82,15 +82,17 @@ __device__ __forceinline__ float4 ld_stream4(const float* p, uint64_t pol) {
 }
 
 // ---- gathered (reused) loads -------------------------------------------------
+// Scalar gathers keep x in L2 (evict-last) but skip L1 allocation: random
+// 8-byte gathers from a multi-MB x hit L1 a few percent of the time.
 __device__ __forceinline__ double ld_keep(const double* p, uint64_t pol) {
   double r;
-  asm("ld.global.nc.L2::cache_hint.f64 %0, [%1], %2;"
+  asm("ld.global.nc.L1::no_allocate.L2::cache_hint.f64 %0, [%1], %2;"
       : "=d"(r) : "l"(p), "l"(pol));
   return r;
 }
 __device__ __forceinline__ float ld_keep(const float* p, uint64_t pol) {
   float r;
-  asm("ld.global.nc.L2::cache_hint.f32 %0, [%1], %2;"
+  asm("ld.global.nc.L1::no_allocate.L2::cache_hint.f32 %0, [%1], %2;"
       : "=f"(r) : "l"(p), "l"(pol));
   return r;
 }
