@@ -14,9 +14,11 @@ Workloads are the seeded benchmark matrices (1 banded, 2 uniform, 3 power-law,
 --auto     choose_spmv's pick against every kernel measured on the device; a
            hit is a pick within 1.1x of the fastest (the reference counts exact
            hits only, bench_main.cpp:229-253); writes results/heuristic.csv
---bench    every kernel: median/min over CUDA-event-timed launches, GFLOP/s,
-           compulsory-traffic GB/s and fraction of the measured HBM peak, and
-           the random-gather ceiling; writes results/bench.csv
+--bench    every kernel: warm median/min per launch over 20 replays of a
+           CUDA graph of 10 launches (one event pair each), cold median per
+           launch after a 256 MB flush, GFLOP/s, compulsory-traffic GB/s and
+           fraction of the measured HBM peak, and the random-gather ceiling;
+           writes results/bench.csv
 --validate every kernel against the bit-exact csr_scalar result of the same
            launch inputs: kernels that keep csr_omp's order must match bit for
            bit, the others must stay within 2*gamma_n*sum|a_ij x_j| per row
@@ -66,21 +68,53 @@ def _bytes(kernel, block, M, A, es):
     return nnz * (es + 4) + (m + 1) * 4 + n * es + m * es
 
 
+_FLUSH = None
+GRAPH_LAUNCHES = 10   # launches captured per graph
+GRAPH_REPLAYS = 20    # timed replays (median reported)
+
+
 def _time(M, x, y, kernel, lanes, block, iters, warmup):
+    """(warm median ms, warm min ms, cold median ms) of one launch.
+
+    Warm: GRAPH_LAUNCHES launches captured once as a CUDA graph, each of
+    GRAPH_REPLAYS replays timed by one event pair (so no host launch gap is
+    counted), median and min over the replays. Cold: one launch right after a
+    write of a 256 MB buffer (twice the L2), median over `iters`; the flush
+    keeps the GPU busy, so the launch starts without a host gap."""
     import torch
-    s = torch.cuda.current_stream()
-    for _ in range(warmup):
-        M.spmv(x, y, kernel=kernel, lanes=lanes, block=block, stream=s)
-    torch.cuda.synchronize()
-    samples = []
-    for _ in range(iters):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(s)
-        M.spmv(x, y, kernel=kernel, lanes=lanes, block=block, stream=s)
-        b.record(s)
-        b.synchronize()
-        samples.append(a.elapsed_time(b))
-    return statistics.median(samples), min(samples)
+    global _FLUSH
+    if _FLUSH is None:
+        _FLUSH = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for _ in range(warmup):
+            M.spmv(x, y, kernel=kernel, lanes=lanes, block=block, stream=s)
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s, capture_error_mode="relaxed"):
+            for _ in range(GRAPH_LAUNCHES):
+                M.spmv(x, y, kernel=kernel, lanes=lanes, block=block, stream=s)
+        g.replay()
+        s.synchronize()
+        warm = []
+        for _ in range(GRAPH_REPLAYS):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(s)
+            g.replay()
+            b.record(s)
+            b.synchronize()
+            warm.append(a.elapsed_time(b) / GRAPH_LAUNCHES)
+        del g
+        cold = []
+        for _ in range(iters):
+            _FLUSH.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(s)
+            M.spmv(x, y, kernel=kernel, lanes=lanes, block=block, stream=s)
+            b.record(s)
+            b.synchronize()
+            cold.append(a.elapsed_time(b))
+    return statistics.median(warm), min(warm), statistics.median(cold)
 
 
 def _setup(which, dtype, seed=2024):
@@ -122,8 +156,8 @@ def _measure_all(which, dtype, iters, warmup):
             continue  # 1M block rows x 50,000-entry rows: blocks would not be the format
         if not _usable(M, k, block):
             continue
-        med, mn = _time(M, x, y, k, lanes, block, iters, warmup)
-        rows.append(dict(kernel=label, id=k, lanes=lanes, block=block, median_ms=med, min_ms=mn,
+        med, mn, cold = _time(M, x, y, k, lanes, block, iters, warmup)
+        rows.append(dict(kernel=label, id=k, lanes=lanes, block=block, median_ms=med, min_ms=mn, cold_ms=cold,
                          gflops=2 * A.nnz / (med * 1e-3) / 1e9, gbs=_bytes(k, block, M, A, es) / (med * 1e-3) / 1e9))
     gather = ctx.gather_rate(A.n, A.nnz)
     return A, rows, gather
@@ -164,7 +198,8 @@ def cmd_bench(args):
             r.update(matrix=WORKLOADS[w], precision=args.dtype, frac_hbm=r["gbs"] / peak,
                      frac_gather=A.nnz / (r["median_ms"] * 1e-3) / gather)
             print(f"  {r['kernel']:16s} {r['median_ms'] * 1e3:9.2f} us  {r['gflops']:8.1f} GFLOP/s "
-                  f"{r['gbs']:8.1f} GB/s  {100 * r['frac_hbm']:5.1f}% HBM  {100 * r['frac_gather']:5.1f}% gather")
+                  f"{r['gbs']:8.1f} GB/s  {100 * r['frac_hbm']:5.1f}% HBM  {100 * r['frac_gather']:5.1f}% gather  "
+                  f"cold {r['cold_ms'] * 1e3:8.2f} us")
             out.append(r)
     _write_csv("bench.csv", out)
     return 0
