@@ -357,7 +357,12 @@ spmvb_status spmvb_dist_enable_peer(spmvb_dist D, void* stream) {
     SPMVB_TRY_CUDA(cudaMemcpyAsync(&all_ok, dok.get(), sizeof(all_ok), cudaMemcpyDeviceToHost, s));
     SPMVB_TRY_CUDA(cudaStreamSynchronize(s));
     if (!all_ok) {
+      // Every rank unmaps the others' buffers; only after all have done so
+      // (the second collective) does a rank free its own.
       D->close_peers();
+      SPMVB_TRY(nccl_enqueued(D->comm, ncclAllReduce(dok.get(), dok.get(), 1, ncclInt32, ncclMin, D->comm, s),
+                              "ncclAllReduce(peer release)"));
+      SPMVB_TRY_CUDA(cudaStreamSynchronize(s));
       D->pmem.reset();
       D->counter.reset();
       return fail(SPMVB_ERR_UNSUPPORTED,
