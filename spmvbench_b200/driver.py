@@ -5,6 +5,7 @@
     python -m spmvbench_b200.driver --auto     [--workload W ...] [--dtype f64|f32]
     python -m spmvbench_b200.driver --bench    [--workload W ...] [--dtype ...] [--iters N]
     python -m spmvbench_b200.driver --validate [--workload W ...]
+    python -m spmvbench_b200.driver --spmm     [--dtype ...] [--k K] [--iters N]
     python -m spmvbench_b200.driver --profile KERNEL --workload W [--steps N] [--warmup N]
 
 Workloads are the seeded benchmark matrices (1 banded, 2 uniform, 3 power-law,
@@ -22,7 +23,14 @@ Workloads are the seeded benchmark matrices (1 banded, 2 uniform, 3 power-law,
 --validate every kernel against the bit-exact csr_scalar result of the same
            launch inputs: kernels that keep csr_omp's order must match bit for
            bit, the others must stay within 2*gamma_n*sum|a_ij x_j| per row
---profile  warmup + steps launches of one kernel on one workload (for ncu)
+--spmm     SpMM Y = A X on the k=64 workload (A = the uniform 1M x 16 matrix,
+           X 1,000,000 x k) for tiles 16/32/64, plain and bucketed, the
+           timings of spmm_csr_tiled (spmm_cuda.cu:215-270: median over
+           `iters` launches after warm-up); GFLOP/s (2*nnz*k), compulsory GB/s
+           (A + X + Y once) and no-reuse GB/s (A + one X row per entry + Y,
+           the traffic when X does not fit in L2); writes results/spmm.csv
+--profile  warmup + steps launches of one kernel on one workload (for ncu);
+           KERNEL `spmm` runs spmvb_spmm (tile 64) with k = --k
 """
 from __future__ import annotations
 
@@ -233,9 +241,72 @@ def cmd_validate(args):
     return 1 if bad else 0
 
 
+def _spmm_setup(which, dtype, k):
+    import torch
+    A = generate(which, seed=2024)
+    npd = np.float64 if dtype == F64 else np.float32
+    ctx = Context(0)
+    M = DeviceMatrix(ctx, A, dtype)
+    X = torch.from_numpy(generate_vector(998, A.n * k).astype(npd).reshape(A.n, k)).cuda()
+    Y = torch.empty(A.m, k, dtype=torch.float64 if dtype == F64 else torch.float32, device="cuda")
+    return ctx, A, M, X, Y
+
+
+def cmd_spmm(args):
+    import torch
+    dtype = F64 if args.dtype == "f64" else F32
+    es = 8 if dtype == F64 else 4
+    peak, src = _peak_gbs()
+    k = args.k
+    _, A, M, X, Y = _spmm_setup(5, dtype, k)
+    a_bytes = A.nnz * (es + 4) + (A.m + 1) * 4
+    comp = a_bytes + A.n * k * es + A.m * k * es
+    noreuse = a_bytes + A.nnz * k * es + A.m * k * es
+    print(f"=== SpMM {WORKLOADS[5]} ({args.dtype}) m={A.m} nnz={A.nnz} k={k}; HBM peak {peak:.0f} GB/s ({src}); "
+          f"X {A.n * k * es / 1e6:.0f} MB ===")
+    out = []
+    for bucketed in (False, True):
+        for tile in (16, 32, 64):
+            for _ in range(args.warmup):
+                M.spmm(X, Y, k, tile=tile, bucketed=bucketed)
+            ts = []
+            for _ in range(args.iters):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                M.spmm(X, Y, k, tile=tile, bucketed=bucketed)
+                b.record()
+                b.synchronize()
+                ts.append(a.elapsed_time(b))
+            med = statistics.median(ts)
+            r = dict(matrix=WORKLOADS[5], precision=args.dtype, k=k, tile=tile, bucketed=int(bucketed),
+                     median_ms=med, min_ms=min(ts), gflops=2 * A.nnz * k / (med * 1e-3) / 1e9,
+                     compulsory_gbs=comp / (med * 1e-3) / 1e9, no_reuse_gbs=noreuse / (med * 1e-3) / 1e9)
+            r["frac_hbm_no_reuse"] = r["no_reuse_gbs"] / peak
+            print(f"  tile {tile:2d} {'bucketed' if bucketed else 'plain   '} {med:8.3f} ms  {r['gflops']:8.1f} GFLOP/s "
+                  f"compulsory {r['compulsory_gbs']:7.1f} GB/s  no-reuse {r['no_reuse_gbs']:7.1f} GB/s "
+                  f"({100 * r['frac_hbm_no_reuse']:5.1f}% HBM)")
+            out.append(r)
+    _write_csv("spmm.csv", out)
+    return 0
+
+
 def cmd_profile(args):
     import torch
     dtype = F64 if args.dtype == "f64" else F32
+    if args.profile == "spmm":
+        _, A, M, X, Y = _spmm_setup(args.workload[0], dtype, args.k)
+        for _ in range(args.warmup):
+            M.spmm(X, Y, args.k, tile=64)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            M.spmm(X, Y, args.k, tile=64)
+        b.record()
+        b.synchronize()
+        print(f"spmm k={args.k} on {WORKLOADS[args.workload[0]]}: "
+              f"{a.elapsed_time(b) / max(1, args.steps) * 1e3:.2f} us per launch "
+              f"({args.steps} launches after {args.warmup} warm-up)")
+        return 0
     ctx, A, M, x, y, _ = _setup(args.workload[0], dtype)
     label = {v[0]: v for v in VARIANTS}
     if args.profile not in label:
@@ -275,12 +346,14 @@ def main(argv=None):
     g.add_argument("--auto", action="store_true")
     g.add_argument("--bench", action="store_true")
     g.add_argument("--validate", action="store_true")
+    g.add_argument("--spmm", action="store_true")
     g.add_argument("--profile", metavar="KERNEL")
     p.add_argument("--workload", type=int, nargs="+", default=[1, 2, 3, 4])
     p.add_argument("--dtype", choices=["f64", "f32"], default="f64")
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--steps", type=int, default=1)
+    p.add_argument("--k", type=int, default=64)
     a = p.parse_args(argv)
     if a.stats:
         return cmd_stats(a)
@@ -290,6 +363,8 @@ def main(argv=None):
         return cmd_bench(a)
     if a.validate:
         return cmd_validate(a)
+    if a.spmm:
+        return cmd_spmm(a)
     return cmd_profile(a)
 
 

@@ -36,3 +36,12 @@ def test_auto_and_profile(tmp_path):
     assert "heuristic-vs-oracle" in out.stdout
     out = run("--profile", "ell", "--workload", "1", "--steps", "2")
     assert out.returncode == 0 and "per launch" in out.stdout, out.stdout + out.stderr
+    out = run("--profile", "spmm", "--workload", "1", "--k", "16", "--steps", "2")
+    assert out.returncode == 0 and "per launch" in out.stdout, out.stdout + out.stderr
+
+
+@pytest.mark.gpu
+def test_spmm_timings(tmp_path):
+    out = run("--spmm", "--k", "8", "--iters", "3", "--warmup", "1", "--dtype", "f32")
+    assert out.returncode == 0, out.stdout + out.stderr
+    assert out.stdout.count("GFLOP/s") == 6 and "wrote results/spmm.csv" in out.stdout
