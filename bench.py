@@ -24,7 +24,8 @@ Extra objects on the same line:
                 reference sources; the C restatement if that is absent) on
                 the same matrix, all host threads, rank 0 at N=1
   e2e           the same metric through the host-buffer API: pinned host x
-                copied in and y copied out every step, inside the timed
+                copied in and y brought out to pinned host memory every
+                step (the SpMV stores y there directly), inside the timed
                 region; the streamed pipeline (spmvb_pipeline_submit, calls
                 overlapped) is the value, spmvb_spmv_host's synchronous call
                 is reported beside it
@@ -400,7 +401,8 @@ def main():
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
     e2e = {"value": world * 2.0 * A.nnz / (e2e_ms * 1e-3) / 1e9, "unit": "GFLOP/s",
            "ms_per_step": e2e_ms, "h2d_bytes_per_step": int(A.n * 8), "d2h_bytes_per_step": int(A.m * 8),
-           "api": "spmvb_pipeline_submit, 3 calls in flight, pinned host x in and y out every step",
+           "api": "spmvb_pipeline_submit, 3 calls in flight; every step copies pinned host x in and the SpMV "
+                  "writes y into pinned host memory",
            "kernel_launches": int(launches_pipe),
            "sync_call": {"value": world * 2.0 * A.nnz / (sync_ms * 1e-3) / 1e9, "ms_per_step": sync_ms,
                          "api": "spmvb_spmv_host"}}

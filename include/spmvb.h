@@ -206,8 +206,11 @@ spmvb_status spmvb_spmv(spmvb_matrix A, spmvb_kernel kernel, int lanes,
                         int block, const void* d_x, void* d_y,
                         spmvb_dtype acc, void* stream);
 /* Same on host buffers: H2D of x, the kernel and D2H of y in stream order,
- * synchronous on return. Replaces set_x + run + result
- * (include/spmvbench/spmv_cuda.cuh:127-135). */
+ * synchronous on return. When h_y is pinned host memory mapped into the
+ * device's address space (cudaHostAlloc / cudaMallocHost, or registered
+ * memory, under unified addressing), every kernel but the merge path stores
+ * y into it directly instead of through a device buffer and a copy.
+ * Replaces set_x + run + result (include/spmvbench/spmv_cuda.cuh:127-135). */
 spmvb_status spmvb_spmv_host(spmvb_matrix A, spmvb_kernel kernel, int lanes,
                              int block, const void* h_x, void* h_y,
                              spmvb_dtype acc, void* stream);
@@ -293,7 +296,9 @@ spmvb_status spmvb_generate_vector(uint64_t seed, int64_t len, double* h_out);
  * synchronously, src/cuda/spmv_cuda.cu:292-330,476-498). A pipeline keeps
  * up to `depth` (1..16) host-buffer SpMVs in flight, each on its own stream
  * and device staging, so with pinned host buffers one call's copy of x in,
- * another's kernel and a third's copy of y out overlap. */
+ * another's kernel and a third's output overlap. y is written by the kernel
+ * straight into a pinned, mapped h_y (all kernels but the merge path), else
+ * staged on the device and copied out. */
 typedef struct spmvb_pipeline_st* spmvb_pipeline;
 spmvb_status spmvb_pipeline_create(spmvb_matrix A, int depth,
                                    spmvb_pipeline* out);

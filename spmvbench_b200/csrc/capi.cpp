@@ -374,6 +374,16 @@ spmvb_status spmvb::check_err_word(spmvb_context ctx, cudaStream_t s) {
   return SPMVB_OK;
 }
 
+void* spmvb::mapped_host_ptr(const void* h) {
+  if (!h) return nullptr;
+  cudaPointerAttributes at{};
+  if (cudaPointerGetAttributes(&at, h) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return at.type == cudaMemoryTypeHost ? at.devicePointer : nullptr;
+}
+
 extern "C" {
 
 static spmvb_status check_pair(spmvb_matrix A, spmvb_dtype acc) {
@@ -421,12 +431,18 @@ spmvb_status spmvb_spmv_host(spmvb_matrix A, spmvb_kernel kernel, int lanes, int
   if ((A->n && !h_x) || (A->m && !h_y)) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null host buffer");
   DeviceGuard g(A->device);
   const size_t xb = size_t(A->n) * dtype_size(A->dtype), yb = size_t(A->m) * dtype_size(acc);
+  // Pinned, mapped y: the kernel stores into it directly (no copy out).
+  void* y_direct = (yb && stores_y_once(kernel)) ? mapped_host_ptr(h_y) : nullptr;
   if (A->stage_in.bytes() < xb + 16) SPMVB_TRY(A->stage_in.alloc(xb + 16));
-  if (A->stage_out.bytes() < yb + 16) SPMVB_TRY(A->stage_out.alloc(yb + 16));
+  if (!y_direct && A->stage_out.bytes() < yb + 16) SPMVB_TRY(A->stage_out.alloc(yb + 16));
   auto s = static_cast<cudaStream_t>(stream);
   if (xb) SPMVB_TRY_CUDA(cudaMemcpyAsync(A->stage_in.get(), h_x, xb, cudaMemcpyHostToDevice, s));
-  SPMVB_TRY(dispatch_spmv(A, kernel, lanes, block, A->stage_in.get(), A->stage_out.get(), acc, s));
-  if (yb) SPMVB_TRY_CUDA(cudaMemcpyAsync(h_y, A->stage_out.get(), yb, cudaMemcpyDeviceToHost, s));
+  if (y_direct) {
+    SPMVB_TRY(dispatch_spmv(A, kernel, lanes, block, A->stage_in.get(), y_direct, acc, s));
+  } else {
+    SPMVB_TRY(dispatch_spmv(A, kernel, lanes, block, A->stage_in.get(), A->stage_out.get(), acc, s));
+    if (yb) SPMVB_TRY_CUDA(cudaMemcpyAsync(h_y, A->stage_out.get(), yb, cudaMemcpyDeviceToHost, s));
+  }
   SPMVB_TRY_CUDA(cudaStreamSynchronize(s));
   return check_err_word(A->ctx, s);
 }

@@ -202,6 +202,17 @@ spmvb_status launch_merge_partition(spmvb_matrix A, cudaStream_t stream);
 // error word; SPMVB_ERR_TIMEOUT if a kernel's bounded wait gave up.
 spmvb_status check_err_word(spmvb_context ctx, cudaStream_t s);
 
+// Host-buffer outputs. A kernel that stores every y element exactly once
+// with a plain store (all but the merge path, whose fix-up pass adds into y)
+// can write y straight into the caller's host buffer when that buffer is
+// pinned and mapped into the current device's address space: the PCIe
+// writes then leave from the SMs as the rows finish, and no device-to-host
+// copy follows the kernel. mapped_host_ptr returns the device address of
+// such a buffer on the current device, or nullptr (pageable memory, device
+// memory, or pinned memory this device cannot address).
+inline bool stores_y_once(spmvb_kernel k) { return k != SPMVB_CSR_MERGE; }
+void* mapped_host_ptr(const void* h);
+
 // Peer-memory exchange launchers (peer.cu).
 spmvb_status peer_launch_ell(spmvb_matrix A, const PeerView& P, const void* x, cudaStream_t s);
 spmvb_status peer_launch_push(spmvb_dtype dtype, const void* y, const PeerView& P, int sm_count, cudaStream_t s);

@@ -7,9 +7,10 @@
 // slot, the copy of the caller's host x in, the SpMV, and the copy of y out,
 // and returns without waiting. Work on one slot is ordered by its stream
 // (its staging is reused only after its previous call has finished), and
-// the slots run side by side: with pinned host buffers one call's copy in,
-// another's kernel and a third's copy out overlap, since the copy engines
-// for the two directions run at once.
+// the slots run side by side: with pinned host buffers one call's copy in
+// overlaps another's kernel and a third's output. When the caller's y is
+// pinned and mapped, kernels that store each y element once write it there
+// directly; otherwise y is staged on the device and copied out.
 #include <cuda_runtime.h>
 
 #include <memory>
@@ -89,9 +90,18 @@ spmvb_status spmvb_pipeline_submit(spmvb_pipeline P, spmvb_kernel kernel, int la
   auto& s = P->slots[P->next];
   P->next = (P->next + 1) % static_cast<int>(P->slots.size());
   const size_t xb = size_t(A->n) * dtype_size(A->dtype), yb = size_t(A->m) * dtype_size(acc);
+  // Pinned, mapped y: the kernel stores into it directly, so only the copy
+  // engine's host-to-device direction is busy and the SpMV's PCIe writes
+  // replace the device-to-host copy (that copy slowed down while a
+  // neighbouring slot's L2-bound SpMV ran).
+  void* y_direct = (yb && stores_y_once(kernel)) ? mapped_host_ptr(h_y) : nullptr;
   if (xb) SPMVB_TRY_CUDA(cudaMemcpyAsync(s.x.get(), h_x, xb, cudaMemcpyHostToDevice, s.stream));
-  SPMVB_TRY(spmvb_spmv(A, kernel, lanes, block, s.x.get(), s.y.get(), acc, s.stream));
-  if (yb) SPMVB_TRY_CUDA(cudaMemcpyAsync(h_y, s.y.get(), yb, cudaMemcpyDeviceToHost, s.stream));
+  if (y_direct) {
+    SPMVB_TRY(spmvb_spmv(A, kernel, lanes, block, s.x.get(), y_direct, acc, s.stream));
+  } else {
+    SPMVB_TRY(spmvb_spmv(A, kernel, lanes, block, s.x.get(), s.y.get(), acc, s.stream));
+    if (yb) SPMVB_TRY_CUDA(cudaMemcpyAsync(h_y, s.y.get(), yb, cudaMemcpyDeviceToHost, s.stream));
+  }
   SPMVB_TRY_CUDA(cudaEventRecord(s.done, s.stream));
   s.used = true;
   return SPMVB_OK;

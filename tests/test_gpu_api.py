@@ -129,6 +129,32 @@ def test_pipeline_streams_host_buffers(ctx, depth):
     P.close()
 
 
+def test_pipeline_every_kernel_pinned_and_pageable_y(ctx):
+    """Pipeline calls on every kernel, y alternating between pinned buffers
+    (written by the kernel directly, except the merge path) and pageable
+    ones (staged and copied), against the device-buffer call bit for bit."""
+    A = S.generate(3, seed=86, scale_rows=50000)
+    M = S.DeviceMatrix(ctx, A, S.F64)
+    x = torch.from_numpy(S.generate_vector(87, A.n)).pin_memory()
+    xd = x.cuda()
+    calls = [(S.CSR_SCALAR, 1, 4), (S.CSR_VECTOR, 8, 4), (S.CSR_WARP, 1, 4), (S.CSR_MERGE, 1, 4),
+             (S.HYB, 1, 4), (S.BCSR, 1, 2), (S.BCSR, 1, 4), (S.CSR_MERGE, 1, 4)]
+    P = S.Pipeline(M, depth=3)
+    outs = []
+    for i, (k, lanes, block) in enumerate(calls):
+        y = (torch.full((A.m,), float("nan"), dtype=torch.float64).pin_memory().numpy() if i % 2 == 0
+             else np.full(A.m, np.nan))
+        P.submit(x.numpy(), y, kernel=k, lanes=lanes, block=block)
+        outs.append(y)
+    P.wait()
+    for (k, lanes, block), y in zip(calls, outs):
+        yd = torch.empty(A.m, dtype=torch.float64, device="cuda")
+        M.spmv(xd, yd, kernel=k, lanes=lanes, block=block)
+        torch.cuda.synchronize()
+        assert_bitwise(yd.cpu().numpy(), y, f"pipeline {S.kernel_name(k)} lanes={lanes} block={block}")
+    P.close()
+
+
 @pytest.mark.parametrize("kernel", ["ELL", "CSR_MERGE", "CSR_SCALAR"])
 def test_single_rank_peer_exchange(ctx, kernel):
     """Peer exchange with one rank: the SpMV writes the next x itself (fused

@@ -194,6 +194,28 @@ def test_host_buffer_entry_point_matches_device(ctx):
         assert_bitwise(run_spmv(M, x, kernel), M.spmv_host(x, kernel=kernel), "host entry")
 
 
+@pytest.mark.parametrize("dtype,acc", DTYPE_PAIRS)
+def test_host_entry_pinned_y_every_kernel(ctx, dtype, acc):
+    """A pinned (mapped) y is written by the kernel itself, every kernel but
+    the merge path; a pageable y goes through the device staging and a copy.
+    Both must equal the device-buffer call bit for bit, on a skewed matrix
+    (long rows cut into HYB segments) as well as a uniform one."""
+    import torch
+    for w, seed in ((2, 57), (3, 58)):
+        A = S.generate(w, seed=seed, scale_rows=60000)
+        x = S.generate_vector(seed + 1, A.n)
+        M = S.DeviceMatrix(ctx, A, dtype)
+        xp = torch.from_numpy(x.astype(NP[dtype])).pin_memory()
+        for kernel, lanes, block, _ in VARIANTS:
+            dev = run_spmv(M, x, kernel, lanes, block, acc)
+            yp = torch.full((A.m,), float("nan"), dtype=torch.float64 if acc == S.F64 else torch.float32).pin_memory()
+            M.spmv_host(xp.numpy(), kernel=kernel, lanes=lanes, block=block, acc=acc, out=yp.numpy())
+            tag = f"w{w} {S.kernel_name(kernel)} lanes={lanes} block={block} {dtype}/{acc}"
+            assert_bitwise(dev, yp.numpy(), tag + " pinned y")
+            y = M.spmv_host(x.astype(NP[dtype]), kernel=kernel, lanes=lanes, block=block, acc=acc)
+            assert_bitwise(dev, y, tag + " pageable y")
+
+
 @pytest.mark.parametrize("K", [-1, 1, 3, 8, 64, 257])
 def test_hyb_widths_are_exact_bounded_and_deterministic(ctx, K):
     """Every width of the hybrid format (-1 = width 0: every row chunked):
