@@ -15,11 +15,14 @@ Workloads are the seeded benchmark matrices (1 banded, 2 uniform, 3 power-law,
 --auto     choose_spmv's pick against every kernel measured on the device; a
            hit is a pick within 1.1x of the fastest (the reference counts exact
            hits only, bench_main.cpp:229-253); writes results/heuristic.csv
---bench    every kernel: warm median/min per launch over 20 replays of a
-           CUDA graph of 10 launches (one event pair each), cold median per
-           launch after a 256 MB flush, GFLOP/s, compulsory-traffic GB/s and
-           fraction of the measured HBM peak, and the random-gather ceiling;
-           writes results/bench.csv
+           with the reference's columns (bench_main.cpp:408-417)
+--bench    every kernel: warm median/min/mean/max per launch over 20 replays
+           of a CUDA graph of 10 launches (one event pair each), cold median
+           per launch after a 256 MB flush, GFLOP/s, compulsory (bw_lo) and
+           no-reuse (bw_hi) GB/s, the fraction of the measured HBM peak, the
+           random-gather ceiling and the transfer time of x in and y out;
+           writes results/bench.csv with the reference's columns first
+           (bench_main.cpp:873-886) and results/gpu_info.txt
 --validate every kernel against the bit-exact csr_scalar result of the same
            launch inputs: kernels that keep csr_omp's order must match bit for
            bit, the others must stay within 2*gamma_n*sum|a_ij x_j| per row
@@ -44,7 +47,7 @@ import sys
 import numpy as np
 
 from . import (BCSR, CSR_MERGE, CSR_SCALAR, CSR_VECTOR, CSR_WARP, ELL, F32, F64, HYB, WORKLOADS,
-               Context, DeviceMatrix, choose_spmv, generate, generate_vector, kernel_name, row_stats)
+               Context, DeviceMatrix, choose_spmv, generate, generate_vector, kernel_name, query_gpu, row_stats)
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
@@ -64,16 +67,56 @@ def _peak_gbs():
     return 6650.0, "fallback"
 
 
-def _bytes(kernel, block, M, A, es):
+def _models(kernel, block, M, A, es):
+    """(compulsory, no-reuse) bytes per launch for the format `kernel` reads:
+    the reference's ByteModel lo / hi (bench_main.cpp:443-457; ELL counts
+    only the real entries and BCSR its block storage, :661-678). lo reads x
+    once; hi fetches an x value (or an x slice per block row) per stored entry."""
     m, n, nnz = A.m, A.n, A.nnz
     if kernel in (ELL, HYB):
-        return nnz * (es + 4) + m * 4 + n * es + m * es
+        base = nnz * (es + 4) + m * 4 + m * es
+        return base + n * es, base + nnz * es
     if kernel == BCSR:
         info = M.info()
         bn = info["bcsr2_block_nnz" if block <= 2 else "bcsr4_block_nnz"]
         b = 2 if block <= 2 else 4
-        return bn * (b * b * es + 4) + ((m + b - 1) // b + 1) * 4 + n * es + m * es
-    return nnz * (es + 4) + (m + 1) * 4 + n * es + m * es
+        base = bn * (b * b * es + 4) + ((m + b - 1) // b + 1) * 4 + m * es
+        return base + n * es, base + bn * b * b * es
+    base = nnz * (es + 4) + (m + 1) * 4 + m * es
+    return base + n * es, base + nnz * es
+
+
+# results/bench.csv: the reference's columns in its order (bench_main.cpp:873-886),
+# then the columns this driver adds.
+BENCH_COLUMNS = ["device", "matrix", "precision", "kernel", "is_baseline", "iters", "median_ms", "min_ms",
+                 "mean_ms", "max_ms", "gflops", "bw_lo_gbs", "bw_hi_gbs", "bw_pct_peak", "transfer_ms",
+                 "speedup", "baseline",
+                 "gpus", "peak_gbs", "roofline_frac", "cold_ms", "gather_frac", "lanes", "block"]
+# results/heuristic.csv: the reference's columns (bench_main.cpp:408-417), then the rule text.
+HEURISTIC_COLUMNS = ["matrix", "device", "chosen", "oracle_best", "chosen_ms", "best_ms", "hit", "slowdown",
+                     "reason"]
+
+
+def bench_row(matrix, precision, label, lanes, block, t, flops, lo, hi, peak, transfer_ms, gather=None,
+              nnz=None):
+    """One results/bench.csv row. `t` holds the timing summary of _time
+    (median/min/mean/max ms per launch, iters, cold ms). bw_pct_peak follows
+    the reference (no-reuse traffic over the peak, in percent); roofline_frac
+    is the compulsory traffic over the peak. No vendor baseline runs on this
+    path, so is_baseline is 0 and speedup / baseline are empty."""
+    med = t["median_ms"]
+    gbs = (lambda b: b / (med * 1e-3) / 1e9) if med > 0 else (lambda b: 0.0)
+    row = {"device": "cuda", "matrix": matrix, "precision": precision, "kernel": label, "is_baseline": 0,
+           "iters": t["iters"], "median_ms": med, "min_ms": t["min_ms"], "mean_ms": t["mean_ms"],
+           "max_ms": t["max_ms"], "gflops": flops / (med * 1e-3) / 1e9 if med > 0 else 0.0,
+           "bw_lo_gbs": gbs(lo), "bw_hi_gbs": gbs(hi), "bw_pct_peak": 100.0 * gbs(hi) / peak if peak else 0.0,
+           "transfer_ms": transfer_ms, "speedup": "", "baseline": "",
+           "gpus": 1, "peak_gbs": peak, "roofline_frac": gbs(lo) / peak if peak else 0.0,
+           "cold_ms": t["cold_ms"],
+           "gather_frac": (nnz / (med * 1e-3) / gather) if (gather and nnz and med > 0) else "",
+           "lanes": lanes, "block": block}
+    assert list(row) == BENCH_COLUMNS
+    return row
 
 
 _FLUSH = None
@@ -82,7 +125,8 @@ GRAPH_REPLAYS = 20    # timed replays (median reported)
 
 
 def _time(M, x, y, kernel, lanes, block, iters, warmup):
-    """(warm median ms, warm min ms, cold median ms) of one launch.
+    """Timing summary of one launch: median / min / mean / max ms over the
+    warm replays (and their count, `iters`), and the cold median `cold_ms`.
 
     Warm: GRAPH_LAUNCHES launches captured once as a CUDA graph, each of
     GRAPH_REPLAYS replays timed by one event pair (so no host launch gap is
@@ -122,7 +166,8 @@ def _time(M, x, y, kernel, lanes, block, iters, warmup):
             b.record(s)
             b.synchronize()
             cold.append(a.elapsed_time(b))
-    return statistics.median(warm), min(warm), statistics.median(cold)
+    return {"median_ms": statistics.median(warm), "min_ms": min(warm), "mean_ms": statistics.fmean(warm),
+            "max_ms": max(warm), "iters": len(warm), "cold_ms": statistics.median(cold)}
 
 
 def _setup(which, dtype, seed=2024):
@@ -155,20 +200,59 @@ def cmd_stats(args):
     return 0
 
 
+def _transfer_ms(x, y, xh, reps=10):
+    """Median of `reps` rounds of one upload of x and one download of y from
+    and to pageable host memory: the reference's transfer_ms
+    (SpmvRunner::measure_transfer_ms, spmv_cuda.cu:340-372), kernel excluded."""
+    import torch
+    hx = torch.from_numpy(np.ascontiguousarray(xh)).to(x.dtype)
+    for _ in range(2):
+        x.copy_(hx)
+        y.cpu()
+    ts = []
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        x.copy_(hx)
+        y.cpu()
+        b.record()
+        b.synchronize()
+        ts.append(a.elapsed_time(b))
+    return statistics.median(ts)
+
+
 def _measure_all(which, dtype, iters, warmup):
-    ctx, A, M, x, y, _ = _setup(which, dtype)
+    """Every usable kernel on workload `which`: a list of (kernel id, bench row)."""
+    ctx, A, M, x, y, xh = _setup(which, dtype)
     es = 8 if dtype == F64 else 4
-    rows = []
+    peak, _ = _peak_gbs()
+    precision = "fp64" if dtype == F64 else "fp32"
+    gather = ctx.gather_rate(A.n, A.nnz)
+    transfer = _transfer_ms(x, y, xh)
+    out = []
     for label, k, lanes, block in VARIANTS:
         if k == BCSR and which == 3:
             continue  # 1M block rows x 50,000-entry rows: blocks would not be the format
         if not _usable(M, k, block):
             continue
-        med, mn, cold = _time(M, x, y, k, lanes, block, iters, warmup)
-        rows.append(dict(kernel=label, id=k, lanes=lanes, block=block, median_ms=med, min_ms=mn, cold_ms=cold,
-                         gflops=2 * A.nnz / (med * 1e-3) / 1e9, gbs=_bytes(k, block, M, A, es) / (med * 1e-3) / 1e9))
-    gather = ctx.gather_rate(A.n, A.nnz)
-    return A, rows, gather
+        t = _time(M, x, y, k, lanes, block, iters, warmup)
+        lo, hi = _models(k, block, M, A, es)
+        out.append((k, bench_row(WORKLOADS[which], precision, label, lanes, block, t, 2.0 * A.nnz, lo, hi, peak,
+                                 transfer, gather, A.nnz)))
+    return A, out, gather
+
+
+def _write_gpu_info(peak, src):
+    """results/gpu_info.txt in the reference's key=value form (bench_main.cpp:888-899)."""
+    g = query_gpu(0)
+    os.makedirs("results", exist_ok=True)
+    with open(os.path.join("results", "gpu_info.txt"), "w") as f:
+        f.write(f"name={g['name']}\ncompute_capability={g['major']}.{g['minor']}\nassumed_peak_gbs={peak}\n"
+                f"peak_source={'measured copy bandwidth (MEASURED_PEAKS.json)' if src == 'measured' else src}\n"
+                f"theoretical_peak_gbs={g['peak_gbs']:.1f}\n"
+                "bandwidth_model=no-reuse (x fetched per nonzero) for bw_hi_gbs and bw_pct_peak; "
+                "compulsory (x once) for bw_lo_gbs and roofline_frac\n"
+                f"sm_count={g['sm_count']}\nl2_bytes={g['l2_bytes']}\nmkl_available=0\n")
 
 
 def cmd_auto(args):
@@ -178,13 +262,16 @@ def cmd_auto(args):
         A, rows, _ = _measure_all(w, dtype, args.iters, args.warmup)
         st = row_stats(A)
         c = choose_spmv(st)
-        best = min(rows, key=lambda r: r["median_ms"])
-        pick = [r for r in rows if r["id"] == c["kernel"] and (c["kernel"] != CSR_VECTOR or r["lanes"] == c["lanes"])
+        best = min((r for _, r in rows), key=lambda r: r["median_ms"])
+        pick = [r for k, r in rows if k == c["kernel"] and (c["kernel"] != CSR_VECTOR or r["lanes"] == c["lanes"])
                 and (c["kernel"] != BCSR or r["block"] == c["block_r"])]
         chosen_ms = pick[0]["median_ms"] if pick else float("nan")
         slow = chosen_ms / best["median_ms"]
-        out.append(dict(matrix=WORKLOADS[w], chosen=c["name"], oracle_best=best["kernel"], chosen_ms=chosen_ms,
-                        best_ms=best["median_ms"], hit=int(slow <= 1.1), slowdown=slow, reason=c["reason"]))
+        row = dict(matrix=WORKLOADS[w], device="cuda", chosen=c["name"], oracle_best=best["kernel"],
+                   chosen_ms=chosen_ms, best_ms=best["median_ms"], hit=int(slow <= 1.1), slowdown=slow,
+                   reason=c["reason"])
+        assert list(row) == HEURISTIC_COLUMNS
+        out.append(row)
         print(f"{WORKLOADS[w]:24s} chosen={c['name']:12s} best={best['kernel']:14s} "
               f"chosen_ms={chosen_ms:.4f} best_ms={best['median_ms']:.4f} slowdown={slow:.3f}")
     hits = sum(r["hit"] for r in out)
@@ -202,14 +289,13 @@ def cmd_bench(args):
         A, rows, gather = _measure_all(w, dtype, args.iters, args.warmup)
         print(f"=== {WORKLOADS[w]} ({args.dtype}) m={A.m} nnz={A.nnz}; HBM peak {peak:.0f} GB/s ({src}), "
               f"gather ceiling {gather / 1e9:.1f} G/s ===")
-        for r in rows:
-            r.update(matrix=WORKLOADS[w], precision=args.dtype, frac_hbm=r["gbs"] / peak,
-                     frac_gather=A.nnz / (r["median_ms"] * 1e-3) / gather)
+        for _, r in rows:
             print(f"  {r['kernel']:16s} {r['median_ms'] * 1e3:9.2f} us  {r['gflops']:8.1f} GFLOP/s "
-                  f"{r['gbs']:8.1f} GB/s  {100 * r['frac_hbm']:5.1f}% HBM  {100 * r['frac_gather']:5.1f}% gather  "
-                  f"cold {r['cold_ms'] * 1e3:8.2f} us")
+                  f"{r['bw_lo_gbs']:8.1f} GB/s  {100 * r['roofline_frac']:5.1f}% HBM  "
+                  f"{100 * r['gather_frac']:5.1f}% gather  cold {r['cold_ms'] * 1e3:8.2f} us")
             out.append(r)
     _write_csv("bench.csv", out)
+    _write_gpu_info(peak, src)
     return 0
 
 

@@ -22,6 +22,39 @@ def test_stats_runs_without_a_gpu():
     assert "banded_100k_hb4" in out.stdout and "dense_share_of_stored_4x4=1" in out.stdout
 
 
+def test_bench_row_has_the_reference_columns_first():
+    """results/bench.csv keeps the reference's columns in its order
+    (bench_main.cpp:873-886) and its definitions: GFLOP/s from 2*nnz, bw_lo
+    (x read once) and bw_hi (x per nonzero) in GB/s, bw_pct_peak from bw_hi."""
+    from spmvbench_b200 import driver as D
+    t = {"median_ms": 0.5, "min_ms": 0.4, "mean_ms": 0.55, "max_ms": 0.7, "iters": 20, "cold_ms": 0.6}
+    r = D.bench_row("m", "fp64", "ell", 1, 4, t, 2e6, 1e9, 3e9, 8000.0, 0.25, gather=1e12, nnz=1e6)
+    ref = ["device", "matrix", "precision", "kernel", "is_baseline", "iters", "median_ms", "min_ms", "mean_ms",
+           "max_ms", "gflops", "bw_lo_gbs", "bw_hi_gbs", "bw_pct_peak", "transfer_ms", "speedup", "baseline"]
+    assert list(r)[:len(ref)] == ref
+    assert r["device"] == "cuda" and r["is_baseline"] == 0 and r["iters"] == 20
+    assert r["gflops"] == pytest.approx(2e6 / 0.5e-3 / 1e9)
+    assert r["bw_lo_gbs"] == pytest.approx(2000.0) and r["bw_hi_gbs"] == pytest.approx(6000.0)
+    assert r["bw_pct_peak"] == pytest.approx(75.0) and r["roofline_frac"] == pytest.approx(0.25)
+    assert r["gather_frac"] == pytest.approx(1e6 / 0.5e-3 / 1e12)
+    assert D.HEURISTIC_COLUMNS[:8] == ["matrix", "device", "chosen", "oracle_best", "chosen_ms", "best_ms",
+                                       "hit", "slowdown"]
+
+
+def test_byte_models_follow_the_reference():
+    """ByteModel lo / hi of bench_main.cpp:443-457 for CSR; ELL counts only the
+    real entries (:661-667)."""
+    from spmvbench_b200 import driver as D
+
+    class A:
+        m, n, nnz = 10, 20, 50
+    lo, hi = D._models(D.CSR_SCALAR, 4, None, A, 8)
+    assert lo == 50 * 12 + 11 * 4 + 20 * 8 + 10 * 8
+    assert hi == 50 * 12 + 11 * 4 + 50 * 8 + 10 * 8
+    lo, hi = D._models(D.ELL, 4, None, A, 8)
+    assert lo == 50 * 12 + 10 * 4 + 10 * 8 + 20 * 8 and hi == 50 * 12 + 10 * 4 + 10 * 8 + 50 * 8
+
+
 @pytest.mark.gpu
 def test_validate_all_workloads(tmp_path):
     out = run("--validate")
@@ -38,6 +71,20 @@ def test_auto_and_profile(tmp_path):
     assert out.returncode == 0 and "per launch" in out.stdout, out.stdout + out.stderr
     out = run("--profile", "spmm", "--workload", "1", "--k", "16", "--steps", "2")
     assert out.returncode == 0 and "per launch" in out.stdout, out.stdout + out.stderr
+
+
+@pytest.mark.gpu
+def test_bench_writes_reference_schema(tmp_path):
+    out = run("--bench", "--workload", "1", "--iters", "3", "--warmup", "1")
+    assert out.returncode == 0, out.stdout + out.stderr
+    import csv as _csv
+    with open(os.path.join(ROOT, "results", "bench.csv")) as f:
+        rows = list(_csv.DictReader(f))
+    assert rows and rows[0]["device"] == "cuda" and rows[0]["matrix"] == "banded_100k_hb4"
+    assert {r["kernel"] for r in rows} >= {"csr_scalar", "csr_vector_l4", "csr_warp", "csr_merge", "ell", "bcsr_4x4"}
+    assert all(float(r["median_ms"]) > 0 and float(r["transfer_ms"]) > 0 for r in rows)
+    info = open(os.path.join(ROOT, "results", "gpu_info.txt")).read()
+    assert "name=" in info and "compute_capability=10.0" in info
 
 
 @pytest.mark.gpu
