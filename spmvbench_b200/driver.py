@@ -8,8 +8,10 @@
     python -m spmvbench_b200.driver --spmm     [--dtype ...] [--k K] [--iters N]
     python -m spmvbench_b200.driver --profile KERNEL --workload W [--steps N] [--warmup N]
 
-Workloads are the seeded benchmark matrices (1 banded, 2 uniform, 3 power-law,
-4 4x4 blocks; see spmvbench_b200.WORKLOADS) instead of .mtx files.
+Matrices: the seeded benchmark workloads (--workload: 1 banded, 2 uniform,
+3 power-law, 4 4x4 blocks, 5 the SpMM matrix; see spmvbench_b200.WORKLOADS),
+or files (--matrix a.mtx b.csrbin ...), or every .mtx file of $SPMVBENCH_DATA
+(default data/) with --all, as the reference's bench takes them.
 
 --stats    row statistics (compute_row_stats fields, bench_main.cpp:102-139)
 --auto     choose_spmv's pick against every kernel measured on the device; a
@@ -47,7 +49,8 @@ import sys
 import numpy as np
 
 from . import (BCSR, CSR_MERGE, CSR_SCALAR, CSR_VECTOR, CSR_WARP, ELL, F32, F64, HYB, WORKLOADS,
-               Context, DeviceMatrix, choose_spmv, generate, generate_vector, kernel_name, query_gpu, row_stats)
+               Context, DeviceMatrix, choose_spmv, generate, generate_vector, kernel_name, query_gpu,
+               read_csr_cache, read_matrix_market, row_stats)
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
@@ -170,9 +173,40 @@ def _time(M, x, y, kernel, lanes, block, iters, warmup):
             "max_ms": max(warm), "iters": len(warm), "cold_ms": statistics.median(cold)}
 
 
-def _setup(which, dtype, seed=2024):
+def _data_dir():
+    """$SPMVBENCH_DATA, else data/ (bench_main.cpp:77-82)."""
+    return os.environ.get("SPMVBENCH_DATA") or "data"
+
+
+def _sources(args):
+    """The matrices a command runs on, as (name, key) pairs: the files named
+    by --matrix (Matrix Market, or a binary CSR cache ending in .csrbin),
+    every .mtx file of the data directory with --all (sorted, as the
+    reference's list_matrices, bench_main.cpp:84-96), else the seeded
+    workloads of --workload. Names are file stems, as in the reference."""
+    if getattr(args, "matrix", None):
+        return [(os.path.splitext(os.path.basename(p))[0], p) for p in args.matrix]
+    if getattr(args, "all", False):
+        d = _data_dir()
+        files = sorted(os.path.join(d, f) for f in os.listdir(d) if f.endswith(".mtx")) if os.path.isdir(d) else []
+        if not files:
+            raise SystemExit(f"no .mtx files found in {d}")
+        return [(os.path.splitext(os.path.basename(p))[0], p) for p in files]
+    return [(WORKLOADS[w], w) for w in args.workload]
+
+
+def _load(key, seed=2024):
+    """CSR of a source key: a seeded workload id, a .csrbin cache or a .mtx file."""
+    if isinstance(key, int):
+        return generate(key, seed=seed)
+    if key.endswith(".csrbin"):
+        return read_csr_cache(key)
+    return read_matrix_market(key)
+
+
+def _setup(key, dtype, seed=2024):
     import torch
-    A = generate(which, seed=seed)
+    A = _load(key, seed)
     xh = generate_vector(999, A.n)
     npd = np.float64 if dtype == F64 else np.float32
     ctx = Context(0)
@@ -192,10 +226,10 @@ def _usable(M, kernel, block):
 
 
 def cmd_stats(args):
-    for w in args.workload:
-        A = generate(w)
+    for name, key in _sources(args):
+        A = _load(key, args.seed)
         s = row_stats(A)
-        print(f"=== {WORKLOADS[w]} ===")
+        print(f"=== {name} ===")
         print("  " + ", ".join(f"{k}={v:.6g}" if isinstance(v, float) else f"{k}={v}" for k, v in s.items()))
     return 0
 
@@ -221,23 +255,23 @@ def _transfer_ms(x, y, xh, reps=10):
     return statistics.median(ts)
 
 
-def _measure_all(which, dtype, iters, warmup):
-    """Every usable kernel on workload `which`: a list of (kernel id, bench row)."""
-    ctx, A, M, x, y, xh = _setup(which, dtype)
+def _measure_all(name, key, dtype, iters, warmup, seed=2024):
+    """Every usable kernel on one matrix: a list of (kernel id, bench row)."""
+    ctx, A, M, x, y, xh = _setup(key, dtype, seed)
     es = 8 if dtype == F64 else 4
     peak, _ = _peak_gbs()
     precision = "fp64" if dtype == F64 else "fp32"
-    gather = ctx.gather_rate(A.n, A.nnz)
+    gather = ctx.gather_rate(max(A.n, 1), max(A.nnz, 1 << 24))  # the probe needs enough gathers to time
     transfer = _transfer_ms(x, y, xh)
     out = []
     for label, k, lanes, block in VARIANTS:
-        if k == BCSR and which == 3:
+        if k == BCSR and key == 3:
             continue  # 1M block rows x 50,000-entry rows: blocks would not be the format
         if not _usable(M, k, block):
             continue
         t = _time(M, x, y, k, lanes, block, iters, warmup)
         lo, hi = _models(k, block, M, A, es)
-        out.append((k, bench_row(WORKLOADS[which], precision, label, lanes, block, t, 2.0 * A.nnz, lo, hi, peak,
+        out.append((k, bench_row(name, precision, label, lanes, block, t, 2.0 * A.nnz, lo, hi, peak,
                                  transfer, gather, A.nnz)))
     return A, out, gather
 
@@ -258,8 +292,8 @@ def _write_gpu_info(peak, src):
 def cmd_auto(args):
     dtype = F64 if args.dtype == "f64" else F32
     out = []
-    for w in args.workload:
-        A, rows, _ = _measure_all(w, dtype, args.iters, args.warmup)
+    for name, key in _sources(args):
+        A, rows, _ = _measure_all(name, key, dtype, args.iters, args.warmup, args.seed)
         st = row_stats(A)
         c = choose_spmv(st)
         best = min((r for _, r in rows), key=lambda r: r["median_ms"])
@@ -267,12 +301,12 @@ def cmd_auto(args):
                 and (c["kernel"] != BCSR or r["block"] == c["block_r"])]
         chosen_ms = pick[0]["median_ms"] if pick else float("nan")
         slow = chosen_ms / best["median_ms"]
-        row = dict(matrix=WORKLOADS[w], device="cuda", chosen=c["name"], oracle_best=best["kernel"],
+        row = dict(matrix=name, device="cuda", chosen=c["name"], oracle_best=best["kernel"],
                    chosen_ms=chosen_ms, best_ms=best["median_ms"], hit=int(slow <= 1.1), slowdown=slow,
                    reason=c["reason"])
         assert list(row) == HEURISTIC_COLUMNS
         out.append(row)
-        print(f"{WORKLOADS[w]:24s} chosen={c['name']:12s} best={best['kernel']:14s} "
+        print(f"{name:24s} chosen={c['name']:12s} best={best['kernel']:14s} "
               f"chosen_ms={chosen_ms:.4f} best_ms={best['median_ms']:.4f} slowdown={slow:.3f}")
     hits = sum(r["hit"] for r in out)
     print(f"heuristic-vs-oracle: {hits}/{len(out)} picks within 1.1x of the fastest; "
@@ -285,9 +319,9 @@ def cmd_bench(args):
     dtype = F64 if args.dtype == "f64" else F32
     peak, src = _peak_gbs()
     out = []
-    for w in args.workload:
-        A, rows, gather = _measure_all(w, dtype, args.iters, args.warmup)
-        print(f"=== {WORKLOADS[w]} ({args.dtype}) m={A.m} nnz={A.nnz}; HBM peak {peak:.0f} GB/s ({src}), "
+    for name, key in _sources(args):
+        A, rows, gather = _measure_all(name, key, dtype, args.iters, args.warmup, args.seed)
+        print(f"=== {name} ({args.dtype}) m={A.m} nnz={A.nnz}; HBM peak {peak:.0f} GB/s ({src}), "
               f"gather ceiling {gather / 1e9:.1f} G/s ===")
         for _, r in rows:
             print(f"  {r['kernel']:16s} {r['median_ms'] * 1e3:9.2f} us  {r['gflops']:8.1f} GFLOP/s "
@@ -302,8 +336,8 @@ def cmd_bench(args):
 def cmd_validate(args):
     import torch
     bad = 0
-    for w in args.workload:
-        ctx, A, M, x, y, xh = _setup(w, F64)
+    for name, key in _sources(args):
+        ctx, A, M, x, y, xh = _setup(key, F64, args.seed)
         M.spmv(x, y, kernel=CSR_SCALAR)
         torch.cuda.synchronize()
         ref = y.cpu().numpy().copy()
@@ -313,7 +347,7 @@ def cmd_validate(args):
         nu = lens * 2.0 ** -53
         bound = 2 * 2 * (nu / (1 - nu)) * abs_sum  # two re-associated sums vs the exact value
         for label, k, lanes, block in VARIANTS:
-            if k == BCSR or (k == ELL and w == 3) or not _usable(M, k, block):
+            if k == BCSR or not _usable(M, k, block):
                 continue  # BCSR re-blocks (validated against its own CPU order in tests/)
             y.fill_(float("nan"))
             M.spmv(x, y, kernel=k, lanes=lanes, block=block)
@@ -321,15 +355,15 @@ def cmd_validate(args):
             got = y.cpu().numpy()
             ok = np.array_equal(got, ref) if k in EXACT else bool(np.all(np.abs(got - ref) <= bound))
             bad += not ok
-            print(f"  {WORKLOADS[w]:24s} {label:16s} {'bit-exact' if k in EXACT else 'gamma_n'}: "
+            print(f"  {name:24s} {label:16s} {'bit-exact' if k in EXACT else 'gamma_n'}: "
                   f"{'ok' if ok else 'FAIL'}")
     print("validate:", "ok" if bad == 0 else f"{bad} failures")
     return 1 if bad else 0
 
 
-def _spmm_setup(which, dtype, k):
+def _spmm_setup(key, dtype, k, seed=2024):
     import torch
-    A = generate(which, seed=2024)
+    A = _load(key, seed)
     npd = np.float64 if dtype == F64 else np.float32
     ctx = Context(0)
     M = DeviceMatrix(ctx, A, dtype)
@@ -344,11 +378,12 @@ def cmd_spmm(args):
     es = 8 if dtype == F64 else 4
     peak, src = _peak_gbs()
     k = args.k
-    _, A, M, X, Y = _spmm_setup(5, dtype, k)
+    name, key = _sources(args)[0] if (args.matrix or args.all) else (WORKLOADS[5], 5)
+    _, A, M, X, Y = _spmm_setup(key, dtype, k, args.seed)
     a_bytes = A.nnz * (es + 4) + (A.m + 1) * 4
     comp = a_bytes + A.n * k * es + A.m * k * es
     noreuse = a_bytes + A.nnz * k * es + A.m * k * es
-    print(f"=== SpMM {WORKLOADS[5]} ({args.dtype}) m={A.m} nnz={A.nnz} k={k}; HBM peak {peak:.0f} GB/s ({src}); "
+    print(f"=== SpMM {name} ({args.dtype}) m={A.m} nnz={A.nnz} k={k}; HBM peak {peak:.0f} GB/s ({src}); "
           f"X {A.n * k * es / 1e6:.0f} MB ===")
     out = []
     for bucketed in (False, True):
@@ -364,7 +399,7 @@ def cmd_spmm(args):
                 b.synchronize()
                 ts.append(a.elapsed_time(b))
             med = statistics.median(ts)
-            r = dict(matrix=WORKLOADS[5], precision=args.dtype, k=k, tile=tile, bucketed=int(bucketed),
+            r = dict(matrix=name, precision=args.dtype, k=k, tile=tile, bucketed=int(bucketed),
                      median_ms=med, min_ms=min(ts), gflops=2 * A.nnz * k / (med * 1e-3) / 1e9,
                      compulsory_gbs=comp / (med * 1e-3) / 1e9, no_reuse_gbs=noreuse / (med * 1e-3) / 1e9)
             r["frac_hbm_no_reuse"] = r["no_reuse_gbs"] / peak
@@ -379,8 +414,9 @@ def cmd_spmm(args):
 def cmd_profile(args):
     import torch
     dtype = F64 if args.dtype == "f64" else F32
+    name, key = _sources(args)[0]
     if args.profile == "spmm":
-        _, A, M, X, Y = _spmm_setup(args.workload[0], dtype, args.k)
+        _, A, M, X, Y = _spmm_setup(key, dtype, args.k, args.seed)
         for _ in range(args.warmup):
             M.spmm(X, Y, args.k, tile=64)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -389,11 +425,11 @@ def cmd_profile(args):
             M.spmm(X, Y, args.k, tile=64)
         b.record()
         b.synchronize()
-        print(f"spmm k={args.k} on {WORKLOADS[args.workload[0]]}: "
+        print(f"spmm k={args.k} on {name}: "
               f"{a.elapsed_time(b) / max(1, args.steps) * 1e3:.2f} us per launch "
               f"({args.steps} launches after {args.warmup} warm-up)")
         return 0
-    ctx, A, M, x, y, _ = _setup(args.workload[0], dtype)
+    ctx, A, M, x, y, _ = _setup(key, dtype, args.seed)
     label = {v[0]: v for v in VARIANTS}
     if args.profile not in label:
         raise SystemExit(f"--profile expects one of {sorted(label)}")
@@ -408,7 +444,7 @@ def cmd_profile(args):
         M.spmv(x, y, kernel=k, lanes=lanes, block=block)
     b.record()
     b.synchronize()
-    print(f"{args.profile} on {WORKLOADS[args.workload[0]]}: {a.elapsed_time(b) / max(1, args.steps) * 1e3:.2f} us "
+    print(f"{args.profile} on {name}: {a.elapsed_time(b) / max(1, args.steps) * 1e3:.2f} us "
           f"per launch ({args.steps} launches after {args.warmup} warm-up)")
     return 0
 
@@ -435,6 +471,10 @@ def main(argv=None):
     g.add_argument("--spmm", action="store_true")
     g.add_argument("--profile", metavar="KERNEL")
     p.add_argument("--workload", type=int, nargs="+", default=[1, 2, 3, 4])
+    p.add_argument("--matrix", nargs="+", metavar="FILE",
+                   help="Matrix Market (.mtx) or CSR-cache (.csrbin) files instead of the seeded workloads")
+    p.add_argument("--all", action="store_true", help="every .mtx file in $SPMVBENCH_DATA (default data/)")
+    p.add_argument("--seed", type=int, default=2024, help="seed of the generated workloads")
     p.add_argument("--dtype", choices=["f64", "f32"], default="f64")
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)

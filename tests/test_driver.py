@@ -11,15 +11,53 @@ import pytest
 from conftest import ROOT
 
 
-def run(*args, timeout=900):
+def run(*args, timeout=900, env=None):
+    e = dict(os.environ, **(env or {}))
     return subprocess.run([sys.executable, "-m", "spmvbench_b200.driver", *args], cwd=ROOT, capture_output=True,
-                          text=True, timeout=timeout)
+                          text=True, timeout=timeout, env=e)
+
+
+MTX = """%%MatrixMarket matrix coordinate real general
+% {name}
+4 4 6
+1 1 2.0
+1 3 -1.0
+2 2 4.0
+3 1 0.5
+3 4 1.5
+4 4 3.0
+"""
 
 
 def test_stats_runs_without_a_gpu():
     out = run("--stats", "--workload", "1", "4")
     assert out.returncode == 0, out.stderr
     assert "banded_100k_hb4" in out.stdout and "dense_share_of_stored_4x4=1" in out.stdout
+
+
+def test_stats_on_matrix_files_and_data_dir(tmp_path):
+    """--matrix FILE and --all ($SPMVBENCH_DATA) take .mtx files, as the
+    reference's bench does (bench_main.cpp:77-96,102-139); a CSR cache file
+    works too; names are the file stems."""
+    import spmvbench_b200 as S
+    for name in ("b_mat", "a_mat"):
+        (tmp_path / f"{name}.mtx").write_text(MTX.format(name=name))
+    (tmp_path / "notes.txt").write_text("not a matrix")
+    out = run("--stats", "--matrix", str(tmp_path / "a_mat.mtx"))
+    assert out.returncode == 0, out.stderr
+    assert "=== a_mat ===" in out.stdout and "nnz=6" in out.stdout and "max_row_nnz=2" in out.stdout
+    out = run("--stats", "--all", env={"SPMVBENCH_DATA": str(tmp_path)})
+    assert out.returncode == 0, out.stderr
+    assert out.stdout.index("=== a_mat ===") < out.stdout.index("=== b_mat ===")
+    assert "notes" not in out.stdout
+    A = S.read_matrix_market(str(tmp_path / "a_mat.mtx"))
+    S.write_csr_cache(str(tmp_path / "a_mat.csrbin"), A)
+    out = run("--stats", "--matrix", str(tmp_path / "a_mat.csrbin"))
+    assert out.returncode == 0 and "nnz=6" in out.stdout, out.stderr
+    empty = tmp_path / "empty"
+    empty.mkdir()
+    out = run("--stats", "--all", env={"SPMVBENCH_DATA": str(empty)})
+    assert out.returncode != 0 and "no .mtx files found" in out.stderr
 
 
 def test_bench_row_has_the_reference_columns_first():
@@ -85,6 +123,15 @@ def test_bench_writes_reference_schema(tmp_path):
     assert all(float(r["median_ms"]) > 0 and float(r["transfer_ms"]) > 0 for r in rows)
     info = open(os.path.join(ROOT, "results", "gpu_info.txt")).read()
     assert "name=" in info and "compute_capability=10.0" in info
+
+
+@pytest.mark.gpu
+def test_auto_and_validate_on_a_matrix_file(tmp_path):
+    (tmp_path / "small.mtx").write_text(MTX.format(name="small"))
+    out = run("--validate", "--matrix", str(tmp_path / "small.mtx"))
+    assert out.returncode == 0 and "validate: ok" in out.stdout, out.stdout + out.stderr
+    out = run("--auto", "--matrix", str(tmp_path / "small.mtx"), "--iters", "3", "--warmup", "1")
+    assert out.returncode == 0 and "small" in out.stdout, out.stdout + out.stderr
 
 
 @pytest.mark.gpu
