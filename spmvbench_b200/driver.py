@@ -23,8 +23,11 @@ or files (--matrix a.mtx b.csrbin ...), or every .mtx file of $SPMVBENCH_DATA
            per launch after a 256 MB flush, GFLOP/s, compulsory (bw_lo) and
            no-reuse (bw_hi) GB/s, the fraction of the measured HBM peak, the
            random-gather ceiling and the transfer time of x in and y out;
-           writes results/bench.csv with the reference's columns first
-           (bench_main.cpp:873-886) and results/gpu_info.txt
+           the reference's vendor baseline row (cusparse_spmv, through
+           torch's sparse CSR SpMV; --no-baseline skips it) and every
+           kernel's speedup over it; writes results/bench.csv with the
+           reference's columns first (bench_main.cpp:873-886) and
+           results/gpu_info.txt
 --validate every kernel against the bit-exact csr_scalar result of the same
            launch inputs: kernels that keep csr_omp's order must match bit for
            bit, the others must stay within 2*gamma_n*sum|a_ij x_j| per row
@@ -204,6 +207,69 @@ def _load(key, seed=2024):
     return read_matrix_market(key)
 
 
+def _time_eager(launch, iters, warmup):
+    """Timing summary of an eager launch (used for the vendor baseline, whose
+    calls allocate and are not captured in a graph): warm = GRAPH_REPLAYS
+    rounds of GRAPH_LAUNCHES back-to-back calls, one event pair per round
+    (host launch gaps included); cold = one call after the L2 flush."""
+    import torch
+    global _FLUSH
+    if _FLUSH is None:
+        _FLUSH = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    for _ in range(warmup):
+        launch()
+    torch.cuda.synchronize()
+    warm, cold = [], []
+    for _ in range(GRAPH_REPLAYS):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(GRAPH_LAUNCHES):
+            launch()
+        b.record()
+        b.synchronize()
+        warm.append(a.elapsed_time(b) / GRAPH_LAUNCHES)
+    for _ in range(iters):
+        _FLUSH.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        launch()
+        b.record()
+        b.synchronize()
+        cold.append(a.elapsed_time(b))
+    return {"median_ms": statistics.median(warm), "min_ms": min(warm), "mean_ms": statistics.fmean(warm),
+            "max_ms": max(warm), "iters": len(warm), "cold_ms": statistics.median(cold)}
+
+
+def _cusparse_row(name, precision, A, M, x, y, dtype, iters, warmup, peak, transfer):
+    """The reference bench's vendor baseline row (cusparse_spmv,
+    bench_main.cpp:643-650): cuSPARSE CSR SpMV through torch's sparse CSR
+    matrix-vector product, timed beside the library's kernels. A comparison
+    only; nothing of the library calls it. None if it cannot run here."""
+    import torch
+    if A.nnz == 0 or A.m == 0:
+        return None
+    try:
+        npd = np.float64 if dtype == F64 else np.float32
+        Ac = torch.sparse_csr_tensor(torch.from_numpy(np.ascontiguousarray(A.rowptr, np.int32)).cuda(),
+                                     torch.from_numpy(np.ascontiguousarray(A.colind, np.int32)).cuda(),
+                                     torch.from_numpy(np.ascontiguousarray(A.values, npd)).cuda(), size=(A.m, A.n))
+        yc = torch.mv(Ac, x)
+        M.spmv(x, y, kernel=CSR_SCALAR)
+        torch.cuda.synchronize()
+        scale = float(y.abs().max()) or 1.0
+        diff = float((yc - y).abs().max()) / scale
+        t = _time_eager(lambda: torch.mv(Ac, x), iters, warmup)
+    except Exception as e:  # noqa: BLE001 - the baseline is optional
+        print(f"  cusparse_spmv: unavailable ({e})")
+        return None
+    es = 8 if dtype == F64 else 4
+    lo, hi = _models(CSR_SCALAR, 4, M, A, es)
+    row = bench_row(name, precision, "cusparse_spmv", 1, 1, t, 2.0 * A.nnz, lo, hi, peak, transfer)
+    row.update(is_baseline=1, baseline="cusparse_spmv")
+    print(f"  cusparse_spmv: max |y - y_csr_scalar| / max|y| = {diff:.2e}")
+    return row
+
+
 def _setup(key, dtype, seed=2024):
     import torch
     A = _load(key, seed)
@@ -255,8 +321,9 @@ def _transfer_ms(x, y, xh, reps=10):
     return statistics.median(ts)
 
 
-def _measure_all(name, key, dtype, iters, warmup, seed=2024):
-    """Every usable kernel on one matrix: a list of (kernel id, bench row)."""
+def _measure_all(name, key, dtype, iters, warmup, seed=2024, baseline=False):
+    """Every usable kernel on one matrix: a list of (kernel id, bench row);
+    with `baseline`, the cuSPARSE row first (kernel id None)."""
     ctx, A, M, x, y, xh = _setup(key, dtype, seed)
     es = 8 if dtype == F64 else 4
     peak, _ = _peak_gbs()
@@ -273,6 +340,12 @@ def _measure_all(name, key, dtype, iters, warmup, seed=2024):
         lo, hi = _models(k, block, M, A, es)
         out.append((k, bench_row(name, precision, label, lanes, block, t, 2.0 * A.nnz, lo, hi, peak,
                                  transfer, gather, A.nnz)))
+    if baseline:
+        cs = _cusparse_row(name, precision, A, M, x, y, dtype, iters, warmup, peak, transfer)
+        if cs is not None:
+            for _, r in out:  # speedup over the vendor baseline, as the reference reports it
+                r.update(baseline="cusparse_spmv", speedup=cs["median_ms"] / r["median_ms"])
+            out.insert(0, (None, cs))
     return A, out, gather
 
 
@@ -320,13 +393,16 @@ def cmd_bench(args):
     peak, src = _peak_gbs()
     out = []
     for name, key in _sources(args):
-        A, rows, gather = _measure_all(name, key, dtype, args.iters, args.warmup, args.seed)
+        A, rows, gather = _measure_all(name, key, dtype, args.iters, args.warmup, args.seed,
+                                       baseline=not args.no_baseline)
         print(f"=== {name} ({args.dtype}) m={A.m} nnz={A.nnz}; HBM peak {peak:.0f} GB/s ({src}), "
               f"gather ceiling {gather / 1e9:.1f} G/s ===")
         for _, r in rows:
+            gf = f"{100 * r['gather_frac']:5.1f}% gather" if r["gather_frac"] != "" else " " * 12
+            sp = f"  {r['speedup']:5.2f}x cuSPARSE" if r["speedup"] != "" else ""
             print(f"  {r['kernel']:16s} {r['median_ms'] * 1e3:9.2f} us  {r['gflops']:8.1f} GFLOP/s "
                   f"{r['bw_lo_gbs']:8.1f} GB/s  {100 * r['roofline_frac']:5.1f}% HBM  "
-                  f"{100 * r['gather_frac']:5.1f}% gather  cold {r['cold_ms'] * 1e3:8.2f} us")
+                  f"{gf}  cold {r['cold_ms'] * 1e3:8.2f} us{sp}")
             out.append(r)
     _write_csv("bench.csv", out)
     _write_gpu_info(peak, src)
@@ -475,6 +551,8 @@ def main(argv=None):
                    help="Matrix Market (.mtx) or CSR-cache (.csrbin) files instead of the seeded workloads")
     p.add_argument("--all", action="store_true", help="every .mtx file in $SPMVBENCH_DATA (default data/)")
     p.add_argument("--seed", type=int, default=2024, help="seed of the generated workloads")
+    p.add_argument("--no-baseline", action="store_true",
+                   help="--bench without the cuSPARSE comparison row (torch's sparse CSR SpMV)")
     p.add_argument("--dtype", choices=["f64", "f32"], default="f64")
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)

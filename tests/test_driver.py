@@ -121,6 +121,9 @@ def test_bench_writes_reference_schema(tmp_path):
     assert rows and rows[0]["device"] == "cuda" and rows[0]["matrix"] == "banded_100k_hb4"
     assert {r["kernel"] for r in rows} >= {"csr_scalar", "csr_vector_l4", "csr_warp", "csr_merge", "ell", "bcsr_4x4"}
     assert all(float(r["median_ms"]) > 0 and float(r["transfer_ms"]) > 0 for r in rows)
+    base = [r for r in rows if r["is_baseline"] == "1"]
+    assert [r["kernel"] for r in base] == ["cusparse_spmv"] and base[0]["speedup"] == ""
+    assert all(r["baseline"] == "cusparse_spmv" and float(r["speedup"]) > 0 for r in rows if r["is_baseline"] == "0")
     info = open(os.path.join(ROOT, "results", "gpu_info.txt")).read()
     assert "name=" in info and "compute_capability=10.0" in info
 
