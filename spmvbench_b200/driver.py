@@ -36,7 +36,9 @@ or files (--matrix a.mtx b.csrbin ...), or every .mtx file of $SPMVBENCH_DATA
            timings of spmm_csr_tiled (spmm_cuda.cu:215-270: median over
            `iters` launches after warm-up); GFLOP/s (2*nnz*k), compulsory GB/s
            (A + X + Y once) and no-reuse GB/s (A + one X row per entry + Y,
-           the traffic when X does not fit in L2); writes results/spmm.csv
+           the traffic when X does not fit in L2), beside the reference's
+           cusparse_spmm baseline (torch's sparse CSR x dense product) and
+           each tile's speedup over it; writes results/spmm.csv
 --profile  warmup + steps launches of one kernel on one workload (for ncu);
            KERNEL `spmm` runs spmvb_spmm (tile 64) with k = --k
 """
@@ -240,6 +242,20 @@ def _time_eager(launch, iters, warmup):
             "max_ms": max(warm), "iters": len(warm), "cold_ms": statistics.median(cold)}
 
 
+def _torch_csr(A, dtype):
+    """A as a torch sparse CSR tensor on the GPU (for the cuSPARSE baselines)."""
+    import warnings
+
+    import torch
+    npd = np.float64 if dtype == F64 else np.float32
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore", UserWarning)  # torch's beta-state notice for sparse CSR
+        return torch.sparse_csr_tensor(torch.from_numpy(np.ascontiguousarray(A.rowptr, np.int32)).cuda(),
+                                       torch.from_numpy(np.ascontiguousarray(A.colind, np.int32)).cuda(),
+                                       torch.from_numpy(np.ascontiguousarray(A.values, npd)).cuda(),
+                                       size=(A.m, A.n), check_invariants=False)
+
+
 def _cusparse_row(name, precision, A, M, x, y, dtype, iters, warmup, peak, transfer):
     """The reference bench's vendor baseline row (cusparse_spmv,
     bench_main.cpp:643-650): cuSPARSE CSR SpMV through torch's sparse CSR
@@ -249,10 +265,7 @@ def _cusparse_row(name, precision, A, M, x, y, dtype, iters, warmup, peak, trans
     if A.nnz == 0 or A.m == 0:
         return None
     try:
-        npd = np.float64 if dtype == F64 else np.float32
-        Ac = torch.sparse_csr_tensor(torch.from_numpy(np.ascontiguousarray(A.rowptr, np.int32)).cuda(),
-                                     torch.from_numpy(np.ascontiguousarray(A.colind, np.int32)).cuda(),
-                                     torch.from_numpy(np.ascontiguousarray(A.values, npd)).cuda(), size=(A.m, A.n))
+        Ac = _torch_csr(A, dtype)
         yc = torch.mv(Ac, x)
         M.spmv(x, y, kernel=CSR_SCALAR)
         torch.cuda.synchronize()
@@ -462,6 +475,38 @@ def cmd_spmm(args):
     print(f"=== SpMM {name} ({args.dtype}) m={A.m} nnz={A.nnz} k={k}; HBM peak {peak:.0f} GB/s ({src}); "
           f"X {A.n * k * es / 1e6:.0f} MB ===")
     out = []
+    base_ms = None
+    if not args.no_baseline and A.nnz > 0:
+        # The reference's SpMM baseline (cusparse_spmm, bench_main.cpp:700-722):
+        # cuSPARSE CSR x dense through torch's sparse CSR product; comparison only.
+        try:
+            Ac = _torch_csr(A, dtype)
+            for _ in range(args.warmup):
+                Yc = torch.sparse.mm(Ac, X)
+            ts = []
+            for _ in range(args.iters):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                Yc = torch.sparse.mm(Ac, X)
+                b.record()
+                b.synchronize()
+                ts.append(a.elapsed_time(b))
+            base_ms = statistics.median(ts)
+            M.spmm(X, Y, k, tile=64)
+            torch.cuda.synchronize()
+            diff = float((Yc - Y).abs().max()) / (float(Y.abs().max()) or 1.0)
+            del Yc, Ac
+            r = dict(matrix=name, precision=args.dtype, k=k, tile="cusparse_spmm", bucketed=0, median_ms=base_ms,
+                     min_ms=min(ts), gflops=2 * A.nnz * k / (base_ms * 1e-3) / 1e9,
+                     compulsory_gbs=comp / (base_ms * 1e-3) / 1e9, no_reuse_gbs=noreuse / (base_ms * 1e-3) / 1e9)
+            r["frac_hbm_no_reuse"] = r["no_reuse_gbs"] / peak
+            r["speedup"] = ""
+            out.append(r)
+            print(f"  cusparse_spmm     {base_ms:8.3f} ms  {r['gflops']:8.1f} GFLOP/s  "
+                  f"(max |Y - Y_tile64| / max|Y| = {diff:.2e})")
+        except Exception as e:  # noqa: BLE001 - the baseline is optional
+            print(f"  cusparse_spmm: unavailable ({e})")
+            base_ms = None
     for bucketed in (False, True):
         for tile in (16, 32, 64):
             for _ in range(args.warmup):
@@ -479,9 +524,11 @@ def cmd_spmm(args):
                      median_ms=med, min_ms=min(ts), gflops=2 * A.nnz * k / (med * 1e-3) / 1e9,
                      compulsory_gbs=comp / (med * 1e-3) / 1e9, no_reuse_gbs=noreuse / (med * 1e-3) / 1e9)
             r["frac_hbm_no_reuse"] = r["no_reuse_gbs"] / peak
+            r["speedup"] = base_ms / med if base_ms else ""
+            sp = f"  {r['speedup']:5.2f}x cuSPARSE" if base_ms else ""
             print(f"  tile {tile:2d} {'bucketed' if bucketed else 'plain   '} {med:8.3f} ms  {r['gflops']:8.1f} GFLOP/s "
                   f"compulsory {r['compulsory_gbs']:7.1f} GB/s  no-reuse {r['no_reuse_gbs']:7.1f} GB/s "
-                  f"({100 * r['frac_hbm_no_reuse']:5.1f}% HBM)")
+                  f"({100 * r['frac_hbm_no_reuse']:5.1f}% HBM){sp}")
             out.append(r)
     _write_csv("spmm.csv", out)
     return 0

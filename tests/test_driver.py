@@ -141,4 +141,5 @@ def test_auto_and_validate_on_a_matrix_file(tmp_path):
 def test_spmm_timings(tmp_path):
     out = run("--spmm", "--k", "8", "--iters", "3", "--warmup", "1", "--dtype", "f32")
     assert out.returncode == 0, out.stdout + out.stderr
-    assert out.stdout.count("GFLOP/s") == 6 and "wrote results/spmm.csv" in out.stdout
+    assert out.stdout.count("GFLOP/s") == 7 and "wrote results/spmm.csv" in out.stdout
+    assert "cusparse_spmm" in out.stdout and out.stdout.count("x cuSPARSE") == 6
