@@ -98,4 +98,19 @@ inline SpmmResult spmm_csr_tiled_f64(const CsrMatrix<double>& A, const std::vect
 
 }  // namespace spmvbench
 
+#ifndef SPMVB_NO_CUSPARSE
+namespace spmvbench {
+// The reference bench's cuSPARSE SpMM baseline (spmm_cuda.cuh:42-49 of
+// SpMVBench): a comparison row, not a library kernel.
+inline SpmmResult cusparse_spmm_f32(const CsrMatrix<float>& A, const std::vector<float>& B, int k, int iters,
+                                    int warmup, std::vector<float>& Y) {
+  return vendor::spmm<SpmmResult>(A, B, k, Y, iters, warmup);
+}
+inline SpmmResult cusparse_spmm_f64(const CsrMatrix<double>& A, const std::vector<double>& B, int k, int iters,
+                                    int warmup, std::vector<double>& Y) {
+  return vendor::spmm<SpmmResult>(A, B, k, Y, iters, warmup);
+}
+}  // namespace spmvbench
+#endif  // SPMVB_NO_CUSPARSE
+
 #endif  // SPMVBENCH_ENABLE_CUDA

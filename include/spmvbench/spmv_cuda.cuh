@@ -216,4 +216,21 @@ class SpmvRunner {
 
 }  // namespace spmvbench
 
+#include "spmvbench/cusparse_baseline.hpp"
+
+#ifndef SPMVB_NO_CUSPARSE
+namespace spmvbench {
+// The reference bench's cuSPARSE SpMV baseline (spmv_cuda.cuh:170-180 of
+// SpMVBench): a comparison row, not a library kernel.
+inline SpmvResult cusparse_spmv_csr_f32(const CsrMatrix<float>& A, const std::vector<float>& x,
+                                        std::vector<float>& y, int iters, int warmup) {
+  return vendor::spmv<SpmvResult>(A, x, y, iters, warmup);
+}
+inline SpmvResult cusparse_spmv_csr_f64(const CsrMatrix<double>& A, const std::vector<double>& x,
+                                        std::vector<double>& y, int iters, int warmup) {
+  return vendor::spmv<SpmvResult>(A, x, y, iters, warmup);
+}
+}  // namespace spmvbench
+#endif  // SPMVB_NO_CUSPARSE
+
 #endif  // SPMVBENCH_ENABLE_CUDA
