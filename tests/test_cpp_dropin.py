@@ -1,10 +1,13 @@
 """The C++ drop-in API (include/spmvbench: CsrMatrix, csr_to_ell,
-csr_to_bcsr, compute_row_stats, choose_spmv, SpmvRunner, spmm_csr_tiled_*)
-exercised by a C++ program written like the reference's own tests
-(tests/cpp/dropin_test.cpp), built against libspmvb.so."""
+csr_to_bcsr, compute_row_stats, choose_spmv, SpmvRunner, spmm_csr_tiled_*,
+the cuSPARSE baselines) exercised by C++ programs written like the
+reference's own tests (tests/cpp/dropin_test.cpp, cusparse_check.cpp), built
+against libspmvb.so; and, where the reference tree is present, the
+reference's own bench program built unmodified against the drop-in."""
 from __future__ import annotations
 
 import os
+import shutil
 import subprocess
 
 import pytest
@@ -31,3 +34,30 @@ def test_dropin_gpu_cases():
     out = subprocess.run([BIN, "gpu"], capture_output=True, text=True, timeout=600)
     assert out.returncode == 0, out.stdout + out.stderr
     assert " 0 failed" in out.stdout
+
+
+REF = os.environ.get("SPMVBENCH_REF", "/root/reference")
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(REF, "bench", "bench_main.cpp")),
+                    reason="the reference tree is absent")
+def test_reference_bench_builds_against_dropin(tmp_path):
+    """The reference's bench_main.cpp, unmodified, with its reader, validator
+    and CPU kernels, compiles and links against include/spmvbench and
+    libspmvb (its src/cuda, formats, stats and select replaced); its --stats
+    and CPU --auto run on a Matrix Market file."""
+    subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "tests", "cpp"), "ref_bench", f"REF={REF}"], check=True)
+    bench = os.path.join(ROOT, "_build", "tests", "ref_bench", "bench")
+    data = tmp_path / "data"
+    data.mkdir()
+    (data / "small.mtx").write_text("%%MatrixMarket matrix coordinate real general\n"
+                                    "4 4 6\n1 1 2.0\n1 3 -1.0\n2 2 4.0\n3 1 0.5\n3 4 1.5\n4 4 3.0\n")
+    out = subprocess.run([bench, "--stats", str(data / "small.mtx")], capture_output=True, text=True, timeout=120,
+                         cwd=tmp_path)
+    assert out.returncode == 0, out.stdout + out.stderr
+    assert "=== small ===" in out.stdout and "rows=4 cols=4 nnz=6" in out.stdout
+    out = subprocess.run([bench, "--auto", "--all", "--cpu"], capture_output=True, text=True, timeout=300,
+                         cwd=tmp_path, env=dict(os.environ, SPMVBENCH_DATA=str(data)))
+    assert out.returncode == 0, out.stdout + out.stderr
+    assert "small" in out.stdout and (tmp_path / "results" / "heuristic.csv").exists()
+    shutil.rmtree(tmp_path / "results")
