@@ -36,6 +36,18 @@ def test_dropin_gpu_cases():
     assert " 0 failed" in out.stdout
 
 
+@pytest.mark.gpu
+def test_cusparse_baselines_agree_with_the_library():
+    """cusparse_spmv_csr_f32/f64 and cusparse_spmm_f32/f64 (the reference
+    bench's comparison rows, as the drop-in provides them) run and agree with
+    SpmvRunner / spmm_csr_tiled within the gamma_n bound."""
+    _build()
+    out = subprocess.run([os.path.join(ROOT, "_build", "tests", "cusparse_check")], capture_output=True, text=True,
+                         timeout=300)
+    assert out.returncode == 0, out.stdout + out.stderr
+    assert " 0 failed" in out.stdout
+
+
 REF = os.environ.get("SPMVBENCH_REF", "/root/reference")
 
 
