@@ -1,10 +1,14 @@
 """Oracle - test infrastructure, never part of the product path.
 
-Two ctypes-loaded libraries built by oracle/Makefile:
-  liboracle.so        C restatement of SpMVBench's CPU path (oracle.c)
-  _ref/libspmvref.so  SpMVBench's own CPU sources compiled in place, plus the
-                      extern "C" shim ref_shim.cpp (present when the
-                      reference tree was available at build time)
+ctypes-loaded libraries built by oracle/Makefile:
+  liboracle.so             C restatement of SpMVBench's CPU path (oracle.c)
+  _ref/libspmvref.so       SpMVBench's own CPU sources compiled in place, plus
+                           the extern "C" shim ref_shim.cpp (present when the
+                           reference tree was available at build time)
+  _ref/libspmvref_cuda.so  SpMVBench's own GPU path (src/cuda) compiled in
+                           place for sm_100a, plus ref_cuda_shim.cu (`make
+                           ref_cuda`), to run the reference's kernels beside
+                           this library's on the same device
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / reference
 arms import this package, and only to check or time: the CUDA library in
@@ -107,6 +111,63 @@ def ref_read_matrix_market(path: str):
     lib.ref_csr_arrays_d(h, _p(rp), _p(ci), _p(va))
     lib.ref_csr_destroy_d(h)
     return m.value, n.value, rp, ci[:nnz.value], va[:nnz.value]
+
+
+REF_CUDA_PATH = os.path.join(_HERE, "_ref", "libspmvref_cuda.so")
+_ref_cuda = None
+
+
+def ref_cuda_available() -> bool:
+    """Whether the reference's own GPU path was built (oracle/Makefile
+    `ref_cuda`: src/cuda compiled for sm_100a)."""
+    return os.path.exists(REF_CUDA_PATH)
+
+
+def ref_cuda() -> C.CDLL:
+    """The reference's GPU path (its SpmvRunner and spmm_csr_tiled) through
+    ref_cuda_shim.cu. Loading needs no GPU; the run functions do, and the
+    reference aborts the process on a CUDA error."""
+    global _ref_cuda
+    if _ref_cuda is None:
+        if not ref_cuda_available():
+            raise ImportError(f"{REF_CUDA_PATH} missing: run `make -C {_HERE} ref_cuda` with the SpMVBench sources")
+        lib = C.CDLL(REF_CUDA_PATH)
+        lib.refcuda_available.restype = C.c_int
+        lib.refcuda_spmv_dd.argtypes = [C.c_int32, C.c_int32, C.c_int64, P, P, P, P, C.c_int, C.c_int, C.c_int,
+                                        C.c_int, C.c_int, P, C.POINTER(C.c_double)]
+        lib.refcuda_spmm_dd.argtypes = [C.c_int32, C.c_int32, C.c_int64, P, P, P, P, C.c_int, C.c_int, C.c_int,
+                                        C.c_int, C.c_int, P, C.POINTER(C.c_double)]
+        _ref_cuda = lib
+    return _ref_cuda
+
+
+def ref_cuda_spmv(m, n, rowptr, colind, vals, x, kernel, lanes=4, block=4, iters=10, warmup=3):
+    """y and the median launch time (ms) of the reference's kernel `kernel`
+    (its KernelId 0..5) on a GPU, fp64."""
+    rp = np.ascontiguousarray(rowptr, np.int32)
+    ci = np.ascontiguousarray(colind, np.int32)
+    va = np.ascontiguousarray(vals, np.float64)
+    xx = np.ascontiguousarray(x, np.float64)
+    y = np.empty(m, np.float64)
+    ms = C.c_double()
+    rc = ref_cuda().refcuda_spmv_dd(m, n, int(rp[m]) if m else 0, _p(rp), _p(ci), _p(va), _p(xx), kernel, lanes,
+                                    block, iters, warmup, _p(y), C.byref(ms))
+    if rc != 0:
+        raise ValueError(f"refcuda_spmv_dd: bad kernel id {kernel}")
+    return y, ms.value
+
+
+def ref_cuda_spmm(m, n, rowptr, colind, vals, B, k, tile=32, balanced=False, iters=10, warmup=3):
+    """Y (m x k) and the median time (ms) of the reference's spmm_csr_tiled_f64."""
+    rp = np.ascontiguousarray(rowptr, np.int32)
+    ci = np.ascontiguousarray(colind, np.int32)
+    va = np.ascontiguousarray(vals, np.float64)
+    BB = np.ascontiguousarray(B, np.float64)
+    Y = np.empty((m, k), np.float64)
+    ms = C.c_double()
+    ref_cuda().refcuda_spmm_dd(m, n, int(rp[m]) if m else 0, _p(rp), _p(ci), _p(va), _p(BB), k, tile, int(balanced),
+                               iters, warmup, _p(Y), C.byref(ms))
+    return Y, ms.value
 
 
 _SUF = {(np.float64, np.float64): "dd", (np.float32, np.float32): "ff", (np.float32, np.float64): "fd"}

@@ -185,3 +185,11 @@ def test_oracle_matches_reference_on_workloads(which, rows):
     lib.ref_row_stats(oracle._p(A.rowptr), oracle._p(A.colind), A.m, A.n, A.nnz, oracle._p(st), None, 0)
     mine = oracle.row_stats(A.m, A.n, A.rowptr, A.colind)
     np.testing.assert_array_equal(np.array([mine[f] for f in oracle.STAT_FIELDS]), st)
+
+
+@pytest.mark.skipif(not oracle.ref_cuda_available(), reason="the reference's GPU path was not built")
+def test_reference_gpu_path_loads():
+    """The reference's src/cuda compiled for sm_100a in place
+    (oracle/_ref/libspmvref_cuda.so, `make -C oracle ref_cuda`) loads, and its
+    gpu_available() answers without aborting where there is no GPU."""
+    assert oracle.ref_cuda().refcuda_available() in (0, 1)
