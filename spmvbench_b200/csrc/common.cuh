@@ -178,20 +178,4 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
   }
   return false;
 }
-// Orders this thread's earlier shared-memory accesses before later
-// async-proxy (TMA) accesses to the same memory.
-__device__ __forceinline__ void fence_proxy_async() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-// 1-D bulk copy global -> shared, completion counted on `bar` in bytes.
-// Both addresses 16-byte aligned, bytes a multiple of 16.
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
-                                         uint32_t bar, uint64_t pol) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
-      "l"(src), "r"(bytes), "r"(bar), "l"(pol)
-      : "memory");
-}
-
 }  // namespace spmvb
