@@ -19,6 +19,7 @@
 // sequential loop ignores them (an error there does not count).
 #include <algorithm>
 #include <cctype>
+#include <cmath>
 #include <charconv>
 #include <cstdio>
 #include <cstring>
@@ -84,7 +85,12 @@ bool parse_ll(const char*& p, const char* e, long long& out) {
 }
 
 // `istream >> double` for decimal numbers: an optional sign, then digits or a
-// point (no inf / nan, which the stream refuses too), correctly rounded.
+// point (no inf / nan, which the stream refuses too), correctly rounded. The
+// stream's extraction (std::num_get) also takes an 'e' / 'E' after the
+// mantissa, with an optional sign and digits, and fails when the collected
+// text is not one complete number: "1.5e" and "1.5e+" are errors, not 1.5.
+// A value too large for a double fails too; one too small for it is read as
+// strtod reads it (zero or a subnormal), as num_get does.
 bool parse_double(const char*& p, const char* e, double& out) {
   while (p < e && is_space(*p)) ++p;
   const char* q = p;
@@ -94,6 +100,12 @@ bool parse_double(const char*& p, const char* e, double& out) {
   double v = 0.0;
   auto r = std::from_chars(q, e, v, std::chars_format::general);
   if (r.ec != std::errc() && r.ec != std::errc::result_out_of_range) return false;
+  if (r.ptr < e && (*r.ptr == 'e' || *r.ptr == 'E')) return false;  // an exponent without digits
+  if (r.ec == std::errc::result_out_of_range) {
+    const std::string text(q, r.ptr);
+    v = std::strtod(text.c_str(), nullptr);
+    if (std::isinf(v)) return false;  // overflow: the stream sets failbit
+  }
   out = neg ? -v : v;
   p = r.ptr;
   return true;
@@ -260,6 +272,14 @@ spmvb_status read_mtx(const std::string& path, int threads, spmvb_host_csr_st& A
   }
   if (count != entries)
     return mm_fail(path, "expected " + std::to_string(entries) + " entries but found " + std::to_string(count));
+
+  // rowptr holds rows + 1 int32 offsets: with 2^31-1 rows that count is not
+  // an int, and the reference's reader fails at this point with the
+  // std::vector length error quoted below (its rows + 1 overflows).
+  if (rows == 2147483647LL)
+    return fail(SPMVB_ERR_INVALID_MATRIX, "Matrix Market: " + path +
+                                              ": 2147483647 rows leave no int32 room for rowptr's rows + 1 "
+                                              "entries (cannot create std::vector larger than max_size())");
 
   // CSR: counting sort by row in file order, then each row sorted by column.
   A.m = static_cast<int32_t>(rows);

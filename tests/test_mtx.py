@@ -206,3 +206,87 @@ def test_csr_cache_rejects_bad_files(tmp_path):
     bad = S.CsrMatrix(2, 2, np.array([0, 2, 1], np.int32), np.array([0, 1], np.int32), np.ones(2))
     with pytest.raises(S.SpmvbError):
         S.write_csr_cache(str(tmp_path / "never.csrbin"), bad)
+
+
+# Value texts around the edges of `istream >> double` (std::num_get): signs,
+# bare points, exponents without digits, overflow and underflow, special
+# names, hexadecimal, separators and trailing text.
+VALUE_FORMS = ["1", "-0", "+3.5", ".5", "5.", "1E-3", "1E+05", "0.1e1", "000001", "-000.000", "-.5e+1",
+               "inf", "-inf", "nan", "NaN", "Infinity", "0x1p3", "1,5", "1_0", "--1", "+.", ".", ".e5", "e5",
+               "1.5e", "1.5E", "1.5e+", "1.5e-", "1.5e++5", "5e", "1.5e5.3", "1.5ex", "1.5x", "1.5 junk",
+               "1e400", "-1e400", "1.8e308", "1.7976931348623158e308", "1e308", "9" * 400,
+               "1e-400", "-1e-400", "4.9e-324", "2.5e-324", "2.4e-324", "1e0000000000000000001",
+               "  7", "7  ", "\t7"]
+
+
+@pytest.mark.parametrize("form", VALUE_FORMS)
+def test_value_forms_match_reference(tmp_path, form):
+    """Each value text either reads as the reference reads it, bit for bit, or
+    fails with the reference's message."""
+    p = write(tmp_path, "v.mtx", f"%%MatrixMarket matrix coordinate real general\n2 2 2\n1 1 {form}\n2 2 2.0\n")
+    try:
+        ref = oracle.ref_read_matrix_market(p)
+        ref_err = None
+    except RuntimeError as e:
+        ref_err = str(e)
+    if ref_err is None:
+        A = S.read_matrix_market(p)
+        assert A.values.tobytes() == ref[4].tobytes()
+    else:
+        with pytest.raises(S.SpmvbError) as ei:
+            S.read_matrix_market(p)
+        assert ref_err in str(ei.value)
+
+
+def _same_outcome(path):
+    """The reference's CSR bit for bit, or its error text within ours."""
+    try:
+        ref = oracle.ref_read_matrix_market(path)
+    except RuntimeError as e:
+        with pytest.raises(S.SpmvbError) as ei:
+            S.read_matrix_market(path)
+        assert str(e) in str(ei.value)
+        return
+    A = S.read_matrix_market(path)
+    assert (A.m, A.n) == ref[:2]
+    np.testing.assert_array_equal(A.rowptr, ref[2])
+    np.testing.assert_array_equal(A.colind, ref[3])
+    assert A.values.tobytes() == ref[4].tobytes()
+
+
+INDEX_FORMS = ["1", "+1", "01", "1.0", "1e0", "-1", "0", "3", "9999999999999999999", "18446744073709551616",
+               "1x", "x", "0x1", " 1"]
+
+
+@pytest.mark.parametrize("form", INDEX_FORMS)
+def test_index_forms_match_reference(tmp_path, form):
+    _same_outcome(write(tmp_path, "r.mtx", f"%%MatrixMarket matrix coordinate real general\n2 2 2\n{form} 1 5.0\n"
+                                           "2 2 2.0\n"))
+    _same_outcome(write(tmp_path, "c.mtx", f"%%MatrixMarket matrix coordinate pattern general\n2 2 2\n1 {form}\n"
+                                           "2 2\n"))
+
+
+SIZE_LINES = ["2 2 2", "2 2", "2", "2 2 2 extra", "-2 2 2", "2 -2 2", "2 2 -2", "2.5 2 2", "2 2 2.5",
+              "99999999999 2 2", "2 99999999999 2", "2147483647 1 0", "2147483648 1 0", "0 0 0", "2 2 3", "2 2 1",
+              "+2 +2 +2", "2e0 2 2", "2 2 9999999999999999999999"]
+
+
+@pytest.mark.parametrize("line", SIZE_LINES)
+def test_size_lines_match_reference(tmp_path, line):
+    _same_outcome(write(tmp_path, "s.mtx", f"%%MatrixMarket matrix coordinate real general\n{line}\n1 1 5.0\n"
+                                           "2 2 2.0\n"))
+
+
+BANNERS = ["%%MatrixMarket matrix coordinate real general", "%%matrixmarket MATRIX Coordinate REAL General",
+           "%%MatrixMarket matrix coordinate real", "%%MatrixMarket matrix coordinate", "%%MatrixMarket matrix",
+           "%%MatrixMarket", "%MatrixMarket matrix coordinate real general",
+           "%%MatrixMarket vector coordinate real general", "%%MatrixMarket matrix array real general",
+           "%%MatrixMarket matrix coordinate complex general", "%%MatrixMarket matrix coordinate real hermitian",
+           "%%MatrixMarket matrix coordinate real skew-symmetric", "%%MatrixMarket matrix coordinate double general",
+           "%%MatrixMarket matrix coordinate real general extra", "  %%MatrixMarket matrix coordinate real general",
+           "%%MatrixMarket  matrix\tcoordinate real general"]
+
+
+@pytest.mark.parametrize("banner", BANNERS)
+def test_banners_match_reference(tmp_path, banner):
+    _same_outcome(write(tmp_path, "b.mtx", f"{banner}\n2 2 2\n1 1 5.0\n2 2 2.0\n"))
