@@ -4,6 +4,11 @@
 //   dropin_test gpu   SpmvRunner / spmm_csr_tiled_* on the device, checked
 //                     like tests/test_cuda_correctness.cpp (gamma_n bound;
 //                     csr_scalar and ELL bit for bit)
+//   dropin_test fuzz LIB  csr_to_ell / csr_to_bcsr<2x2, 4x4> on random
+//                     matrices against the reference's own conversions in
+//                     LIB (oracle/_ref/libspmvref.so), bit for bit
+#include <dlfcn.h>
+
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -163,9 +168,79 @@ static void gpu_tests() {
     }
 }
 
+// Random CSR: empty rows, unsorted and repeated columns, long rows, tails
+// that leave partial 2x2 / 4x4 blocks.
+static CsrMatrix<double> random_matrix(std::mt19937_64& rng) {
+  const int m = static_cast<int>(rng() % 37), n = 1 + static_cast<int>(rng() % 45);
+  CsrMatrix<double> A(m, n);
+  for (int i = 0; i < m; ++i) {
+    const int kind = static_cast<int>(rng() % 5);
+    const int len = kind == 0 ? 0 : kind == 1 ? static_cast<int>(rng() % (2 * n + 1)) : static_cast<int>(rng() % 6);
+    for (int j = 0; j < len; ++j) {
+      A.colind.push_back(static_cast<Index>(rng() % n));
+      A.values.push_back(static_cast<double>(static_cast<int64_t>(rng() % 2001) - 1000) / 7.0);
+    }
+    A.rowptr[i + 1] = static_cast<Index>(A.colind.size());
+  }
+  A.nnz = A.rowptr[m];
+  return A;
+}
+
+template <int B>
+static void fuzz_bcsr(void* lib, void* h, const CsrMatrix<double>& A) {
+  auto shape = reinterpret_cast<void (*)(void*, int, int32_t*, int64_t*)>(dlsym(lib, "ref_bcsr_shape_d"));
+  auto conv = reinterpret_cast<void (*)(void*, int, int32_t*, int32_t*, double*)>(dlsym(lib, "ref_csr_to_bcsr_d"));
+  int32_t mb = 0;
+  int64_t bn = 0;
+  shape(h, B, &mb, &bn);
+  std::vector<int32_t> rp(mb + 1), ci(bn > 0 ? bn : 1);
+  std::vector<double> v((bn > 0 ? bn : 1) * B * B);
+  conv(h, B, rp.data(), ci.data(), v.data());
+  const auto mine = csr_to_bcsr<double, B, B>(A);
+  EXPECT(mine.mb == mb && mine.block_nnz == bn);
+  EXPECT(std::vector<int32_t>(mine.rowptr.begin(), mine.rowptr.end()) == rp);
+  EXPECT(std::vector<int32_t>(mine.colind.begin(), mine.colind.end()) == std::vector<int32_t>(ci.begin(), ci.begin() + bn));
+  EXPECT(mine.values == std::vector<double>(v.begin(), v.begin() + bn * B * B));
+}
+
+static void fuzz_tests(const char* libpath) {
+  void* lib = dlopen(libpath, RTLD_NOW | RTLD_LOCAL);
+  if (!lib) {
+    std::printf("FAIL cannot load %s: %s\n", libpath, dlerror());
+    ++g_fail;
+    return;
+  }
+  auto create = reinterpret_cast<void* (*)(int32_t, int32_t, int64_t, const int32_t*, const int32_t*, const double*)>(
+      dlsym(lib, "ref_csr_create_d"));
+  auto destroy = reinterpret_cast<void (*)(void*)>(dlsym(lib, "ref_csr_destroy_d"));
+  auto width = reinterpret_cast<int32_t (*)(void*)>(dlsym(lib, "ref_ell_width_d"));
+  auto to_ell = reinterpret_cast<void (*)(void*, int32_t*, double*, int32_t*)>(dlsym(lib, "ref_csr_to_ell_d"));
+  std::mt19937_64 rng(20241202);
+  for (int t = 0; t < 400; ++t) {
+    const CsrMatrix<double> A = random_matrix(rng);
+    void* h = create(A.m, A.n, A.nnz, A.rowptr.data(), A.colind.data(), A.values.data());
+    const int32_t w = width(h);
+    std::vector<int32_t> ec(static_cast<size_t>(A.m) * w + 1), rl(A.m + 1);
+    std::vector<double> ev(static_cast<size_t>(A.m) * w + 1);
+    to_ell(h, ec.data(), ev.data(), rl.data());
+    const auto mine = csr_to_ell(A);
+    const size_t slots = static_cast<size_t>(A.m) * w;
+    EXPECT(mine.max_row_nnz == w);
+    EXPECT(std::vector<int32_t>(mine.colind.begin(), mine.colind.end()) ==
+           std::vector<int32_t>(ec.begin(), ec.begin() + slots));
+    EXPECT(mine.values == std::vector<double>(ev.begin(), ev.begin() + slots));
+    EXPECT(mine.row_lengths == std::vector<int>(rl.begin(), rl.begin() + A.m));
+    fuzz_bcsr<2>(lib, h, A);
+    fuzz_bcsr<4>(lib, h, A);
+    destroy(h);
+  }
+  dlclose(lib);
+}
+
 int main(int argc, char** argv) {
   const std::string mode = argc > 1 ? argv[1] : "cpu";
   if (mode == "cpu") cpu_tests();
+  else if (mode == "fuzz") fuzz_tests(argc > 2 ? argv[2] : "");
   else gpu_tests();
   std::printf("%d passed, %d failed\n", g_pass, g_fail);
   return g_fail == 0 ? 0 : 1;

@@ -28,6 +28,19 @@ def test_dropin_cpu_cases():
     assert " 0 failed" in out.stdout
 
 
+def test_dropin_conversions_match_reference_on_random_matrices():
+    """The drop-in's header-only csr_to_ell and csr_to_bcsr<2,2> / <4,4> on 400
+    random matrices (empty rows, unsorted and repeated columns, partial blocks)
+    against the reference's own conversions (oracle/_ref), bit for bit."""
+    import oracle
+    if not oracle.ref_available():
+        pytest.skip("oracle/_ref not built")
+    _build()
+    out = subprocess.run([BIN, "fuzz", oracle.REF_PATH], capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stdout + out.stderr
+    assert " 0 failed" in out.stdout
+
+
 @pytest.mark.gpu
 def test_dropin_gpu_cases():
     _build()
