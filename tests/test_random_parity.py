@@ -6,8 +6,8 @@ entries, tails that cut 2x2 / 4x4 blocks - each checked for:
   * spmvb_compute_row_stats against compute_row_stats, every field bit for
     bit, and the histogram;
   * spmvb_choose_spmv_reference against choose_spmv on those statistics;
-  * the oracle's csr_omp, ELL and BCSR conversions and kernels against the
-    reference's, bit for bit.
+  * the oracle's csr_omp, spmm_csr_cpu, ELL and BCSR conversions and kernels
+    against the reference's, bit for bit.
 CPU only; skipped where oracle/_ref is absent.
 """
 from __future__ import annotations
@@ -87,6 +87,9 @@ def test_random_matrices_match_reference(seed):
         x = rng.uniform(-1, 1, n)
         R = oracle.RefCsr(m, n, rp, ci, va)
         np.testing.assert_array_equal(oracle.spmv_csr(m, rp, ci, va, x, np.float64), R.spmv(x))
+        k = int(rng.integers(1, 9))
+        B = rng.uniform(-1, 1, (n, k))
+        np.testing.assert_array_equal(oracle.spmm_csr(m, k, rp, ci, va, B, np.float64), R.spmm(B, k))
         w, ecol, ev, rl = oracle.csr_to_ell(m, rp, ci, va)
         assert w == lib.ref_ell_width_d(R.h)
         recol = np.zeros(max(m * w, 1), np.int32)
