@@ -136,7 +136,8 @@ typedef struct spmvb_choice {
 const char* spmvb_version(void);
 const char* spmvb_last_error(void);
 const char* spmvb_status_string(spmvb_status s);
-/* Kernel launches issued by this library since load (all devices). */
+/* Kernel launches issued by this library since load (all devices). No
+ * reference counterpart (the bench reports it as its launch count). */
 uint64_t spmvb_launch_count(void);
 
 /* Replaces gpu_available() (include/spmvbench/spmv_cuda.cuh:110): never aborts. */
@@ -178,11 +179,15 @@ spmvb_status spmvb_csr_validate(int32_t m, int32_t n, int64_t nnz,
                                 int32_t* max_row_nnz);
 /* Build what `kernel` needs (ELL, HYB, BCSR `block`, merge-path partition)
  * ahead of the first call; kernel = -1 builds the SpMM row-length buckets.
+ * Replaces the eager conversions and uploads of SpmvRunner's constructor
+ * (src/cuda/spmv_cuda.cu:234-291), done here per format and on demand.
  * param: block size for SPMVB_BCSR, forced width K for SPMVB_HYB
  * (0 = automatic). Lazy builds synchronize the device, so call this before
  * capturing a stream into a CUDA graph. */
 spmvb_status spmvb_matrix_prepare(spmvb_matrix A, spmvb_kernel kernel,
                                   int param);
+/* Sizes of the formats built so far. Replaces SpmvRunner::ell_padded_nnz /
+ * ell_touched_nnz / bcsr_block_nnz (include/spmvbench/spmv_cuda.cuh:137-140). */
 spmvb_status spmvb_matrix_get_info(spmvb_matrix A, spmvb_matrix_info* out);
 
 /* Download a device-built format in the reference host layout, for
@@ -346,6 +351,8 @@ spmvb_status spmvb_host_csr_get(spmvb_host_csr A, int32_t* m, int32_t* n,
 void spmvb_host_csr_free(spmvb_host_csr A);
 
 /* ---- multi-GPU row sharding ---------------------------------------------------- */
+/* No reference counterpart: SpMVBench runs on one GPU. These entry points add
+ * the row-sharded multi-GPU SpMV (one process per GPU) and its x exchange. */
 /* nnz-balanced contiguous row blocks: bounds[g] = lower_bound(rowptr,
  * ceil(g*nnz/parts)) for g in 1..parts-1, bounds[0]=0, bounds[parts]=m. */
 spmvb_status spmvb_partition_rows(const int32_t* h_rowptr, int32_t m,
