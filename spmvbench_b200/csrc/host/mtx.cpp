@@ -393,6 +393,23 @@ spmvb_status spmvb_csr_cache_read(const char* path, spmvb_host_csr* out) {
     std::fclose(f);
     return fail(SPMVB_ERR_INVALID_MATRIX, std::string(path) + ": not a CSR cache file of this version");
   }
+  // The header's sizes must account for the whole file before anything is
+  // allocated: a damaged header cannot make the reader claim (and zero) more
+  // memory than the file holds.
+  const long long expect = static_cast<long long>(sizeof(h)) + (static_cast<long long>(h.m) + 1) * 4 +
+                           static_cast<long long>(h.nnz) * 12;
+  if (std::fseek(f, 0, SEEK_END) != 0) {
+    std::fclose(f);
+    return fail(SPMVB_ERR_IO, std::string(path) + ": cannot determine the file size");
+  }
+  const long long size = std::ftell(f);
+  if (size != expect) {
+    std::fclose(f);
+    return fail(SPMVB_ERR_INVALID_MATRIX, std::string(path) + ": truncated CSR cache file (" +
+                                              std::to_string(size) + " bytes, the header describes " +
+                                              std::to_string(expect) + ")");
+  }
+  std::fseek(f, static_cast<long>(sizeof(h)), SEEK_SET);
   auto A = std::make_unique<spmvb_host_csr_st>();
   A->m = h.m;
   A->n = h.n;

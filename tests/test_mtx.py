@@ -203,6 +203,51 @@ def test_csr_cache_rejects_bad_files(tmp_path):
     with pytest.raises(S.SpmvbError) as e:
         S.read_csr_cache(str(tmp_path / "missing.csrbin"))
     assert e.value.status == 9
+
+
+def test_csr_cache_header_cannot_claim_more_than_the_file(tmp_path):
+    """A damaged header (nnz or m near 2^31) in a small file is refused from
+    the file size before any allocation, not after zeroing tens of GB."""
+    import struct
+    import time
+    A = S.generate(1, seed=4, scale_rows=200)
+    p = tmp_path / "a.csrbin"
+    S.write_csr_cache(str(p), A)
+    raw = bytearray(p.read_bytes())
+    for off, fmt, value in ((24, "<q", 2**31 - 1), (16, "<i", 2**31 - 2)):  # nnz, m
+        bad = bytearray(raw)
+        struct.pack_into(fmt, bad, off, value)
+        q = tmp_path / f"big{off}.csrbin"
+        q.write_bytes(bytes(bad))
+        t0 = time.perf_counter()
+        with pytest.raises(S.SpmvbError, match="truncated") as e:
+            S.read_csr_cache(str(q))
+        assert e.value.status == 2 and time.perf_counter() - t0 < 1.0
+
+
+def test_csr_cache_random_damage(tmp_path):
+    """Truncations and byte flips anywhere: every read either fails with an
+    error status or returns a CSR that passes validation."""
+    A = S.generate(1, seed=5, scale_rows=300)
+    p = tmp_path / "a.csrbin"
+    S.write_csr_cache(str(p), A)
+    raw = p.read_bytes()
+    rng = np.random.default_rng(6)
+    q = tmp_path / "f.csrbin"
+    for t in range(600):
+        b = bytearray(raw)
+        if t % 3 == 0:
+            b = b[: int(rng.integers(0, len(b)))]
+        else:
+            lo = 0 if t % 3 == 1 else 40
+            for _ in range(int(rng.integers(1, 5))):
+                b[int(rng.integers(lo if lo < len(b) else 0, len(b)))] = int(rng.integers(0, 256))
+        q.write_bytes(bytes(b))
+        try:
+            B = S.read_csr_cache(str(q))
+        except S.SpmvbError:
+            continue
+        S.csr_validate(B)
     bad = S.CsrMatrix(2, 2, np.array([0, 2, 1], np.int32), np.array([0, 1], np.int32), np.ones(2))
     with pytest.raises(S.SpmvbError):
         S.write_csr_cache(str(tmp_path / "never.csrbin"), bad)
