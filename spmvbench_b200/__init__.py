@@ -41,6 +41,36 @@ def _ptr(a: np.ndarray):
     return a.ctypes.data_as(C.c_void_p) if a is not None and a.size else None
 
 
+def _int32(a, what: str) -> np.ndarray:
+    """`a` as a contiguous int32 array; integer values outside int32 are an
+    error instead of wrapping."""
+    arr = np.asarray(a)
+    if arr.dtype != np.int32 and arr.dtype.kind in "iu" and arr.size and \
+            (int(arr.min()) < -2**31 or int(arr.max()) > 2**31 - 1):
+        raise ValueError(f"{what} has values outside the int32 index range")
+    return np.ascontiguousarray(arr, np.int32)
+
+
+def _csr_buffers(A: "CsrMatrix", value_dtype=None):
+    """Contiguous int32 rowptr and colind of A (and its values as
+    `value_dtype`), with their lengths checked against m and rowptr[m]: the C
+    ABI takes plain pointers and reads m + 1 and nnz entries through them, so a
+    short array here would be read past its end."""
+    rp = _int32(A.rowptr, "rowptr")
+    if rp.ndim != 1 or rp.size < A.m + 1:
+        raise ValueError(f"rowptr holds {rp.size} entries; m + 1 = {A.m + 1} are needed")
+    nnz = int(rp[A.m]) if A.m else 0
+    ci = _int32(A.colind, "colind")
+    if ci.size < nnz:
+        raise ValueError(f"colind holds {ci.size} entries; rowptr[m] = {nnz} are needed")
+    if value_dtype is None:
+        return rp, ci
+    va = np.ascontiguousarray(A.values, value_dtype)
+    if va.size < nnz:
+        raise ValueError(f"values holds {va.size} entries; rowptr[m] = {nnz} are needed")
+    return rp, ci, va
+
+
 @dataclass
 class CsrMatrix:
     """Host CSR with int32 indices (reference CsrMatrix<T>)."""
@@ -107,9 +137,7 @@ def read_matrix_market(path: str, threads: int = 0) -> CsrMatrix:
 
 def write_csr_cache(path: str, A: CsrMatrix) -> None:
     """Binary CSR cache of A (validated), read back by read_csr_cache."""
-    rp = np.ascontiguousarray(A.rowptr, np.int32)
-    ci = np.ascontiguousarray(A.colind, np.int32)
-    va = np.ascontiguousarray(A.values, np.float64)
+    rp, ci, va = _csr_buffers(A, np.float64)
     call("spmvb_csr_cache_write", os.fsencode(path), A.m, A.n, A.nnz, _ptr(rp), _ptr(ci), _ptr(va))
 
 
@@ -147,8 +175,7 @@ def kernel_name(k: int) -> str:
 
 def row_stats(A: CsrMatrix, histogram: bool = False) -> dict:
     s = _lib.RowStats()
-    rp = np.ascontiguousarray(A.rowptr, np.int32)
-    ci = np.ascontiguousarray(A.colind, np.int32)
+    rp, ci = _csr_buffers(A)
     hist = None
     if histogram:
         mx = int(np.max(np.diff(rp))) if A.m else 0
@@ -194,8 +221,7 @@ def partition_rows(rowptr: np.ndarray, parts: int) -> np.ndarray:
 
 def csr_validate(A: CsrMatrix) -> int:
     """Host validation of a CSR (raises SpmvbError); returns the longest row."""
-    rp = np.ascontiguousarray(A.rowptr, np.int32)
-    ci = np.ascontiguousarray(A.colind, np.int32)
+    rp, ci = _csr_buffers(A)
     mx = C.c_int32()
     call("spmvb_csr_validate", A.m, A.n, A.nnz, _ptr(rp), _ptr(ci), C.byref(mx))
     return mx.value
@@ -204,8 +230,7 @@ def csr_validate(A: CsrMatrix) -> int:
 def shard_csr(A: CsrMatrix, bounds: np.ndarray, rank: int):
     """Rank `rank`'s rows of a square CSR with columns renumbered into the
     padded gather layout. Returns (max_rows, local rowptr, local colind)."""
-    rp = np.ascontiguousarray(A.rowptr, np.int32)
-    ci = np.ascontiguousarray(A.colind, np.int32)
+    rp, ci = _csr_buffers(A)
     b = np.ascontiguousarray(bounds, np.int32)
     nranks = b.size - 1
     mr, ln = C.c_int32(), C.c_int64()
@@ -270,9 +295,7 @@ class DeviceMatrix:
         self.ctx = ctx
         self.m, self.n, self.nnz = A.m, A.n, A.nnz
         self.dtype = dtype
-        rp = np.ascontiguousarray(A.rowptr, np.int32)
-        ci = np.ascontiguousarray(A.colind, np.int32)
-        va = np.ascontiguousarray(A.values, _np_dtype(dtype))
+        rp, ci, va = _csr_buffers(A, _np_dtype(dtype))
         h = C.c_void_p()
         call("spmvb_matrix_create_csr", ctx.handle, dtype, A.m, A.n, A.nnz, _ptr(rp), _ptr(ci),
              _ptr(va), C.byref(h))
@@ -395,9 +418,7 @@ class DistMatrix:
 
     def __init__(self, ctx: Context, nranks: int, rank: int, uid: bytes | None, A: CsrMatrix,
                  bounds: np.ndarray, dtype: int = F64):
-        rp = np.ascontiguousarray(A.rowptr, np.int32)
-        ci = np.ascontiguousarray(A.colind, np.int32)
-        va = np.ascontiguousarray(A.values, _np_dtype(dtype))
+        rp, ci, va = _csr_buffers(A, _np_dtype(dtype))
         b = np.ascontiguousarray(bounds, np.int32)
         ub = C.create_string_buffer(uid, 128) if uid is not None else None
         h = C.c_void_p()

@@ -70,6 +70,56 @@ def test_validation_rejects_bad_csr(A, what):
     assert e.value.status == 2 and what in str(e.value)
 
 
+def test_short_or_out_of_range_arrays_are_refused_before_the_c_call():
+    """The C ABI reads m + 1 rowptr and rowptr[m] colind / values entries
+    through plain pointers; the Python layer refuses shorter arrays (and
+    integer indices outside int32) before handing them over."""
+    cases = [
+        S.CsrMatrix(3, 4, np.array([0, 1, 2], np.int32), np.array([0, 1], np.int32), np.ones(2)),   # rowptr short
+        S.CsrMatrix(2, 4, np.array([0, 2, 5], np.int32), np.array([0, 1, 2], np.int32), np.ones(5)),  # colind short
+        S.CsrMatrix(2, 4, np.array([0, 1, 2], np.int64), np.array([0, 2**33], np.int64), np.ones(2)),  # > int32
+    ]
+    for A in cases:
+        with pytest.raises(ValueError):
+            S.csr_validate(A)
+        with pytest.raises(ValueError):
+            S.row_stats(A)
+    A = S.CsrMatrix(2, 4, np.array([0, 1, 2], np.int32), np.array([0, 1], np.int32), np.ones(1))  # values short
+    with pytest.raises(ValueError):
+        S.write_csr_cache("/nonexistent/never.csrbin", A)
+
+
+def test_validation_agrees_with_the_csr_rules_on_random_damage():
+    """spmvb_csr_validate accepts exactly the CSRs that satisfy rowptr[0] = 0,
+    non-decreasing rowptr, rowptr[m] entries in colind, and every column in
+    [0, n) (longer arrays are allowed; the tail is not read)."""
+    rng = np.random.default_rng(11)
+    for t in range(3000):
+        m, n = int(rng.integers(0, 8)), int(rng.integers(0, 8))
+        rp = np.zeros(m + 1, np.int64)
+        rp[1:] = np.cumsum(rng.integers(0, 4, m))
+        ci = rng.integers(0, max(n, 1), int(rp[-1])).astype(np.int64)
+        k = t % 6
+        if k == 1 and m:
+            rp[rng.integers(0, m + 1)] += int(rng.integers(-3, 4))
+        if k == 2 and ci.size:
+            ci[rng.integers(0, ci.size)] = int(rng.integers(-3, n + 3))
+        if k == 3:
+            rp[0] = int(rng.integers(-2, 3))
+        if k == 4 and ci.size:
+            ci = ci[:-1]
+        nnz = int(rp[m]) if m else 0
+        valid = (rp[0] == 0 and bool(np.all(np.diff(rp) >= 0)) and 0 <= nnz <= ci.size
+                 and (nnz == 0 or (ci[:nnz].min() >= 0 and ci[:nnz].max() < n)))
+        A = S.CsrMatrix(m, n, rp.astype(np.int32), ci.astype(np.int32), np.zeros(ci.size))
+        try:
+            S.csr_validate(A)
+            got = True
+        except (S.SpmvbError, ValueError):
+            got = False
+        assert got == valid, (m, n, rp.tolist(), ci.tolist())
+
+
 def test_validation_rejects_nnz_mismatch():
     A = S.CsrMatrix(2, 2, np.array([0, 1, 2], np.int32), np.array([0, 1], np.int32), np.ones(2))
     lib = S.load()
