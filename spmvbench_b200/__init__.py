@@ -41,6 +41,26 @@ def _ptr(a: np.ndarray):
     return a.ctypes.data_as(C.c_void_p) if a is not None and a.size else None
 
 
+def _host_in(a, dtype, count: int, what: str) -> np.ndarray:
+    """A host input the C ABI reads `count` entries of, as a contiguous array
+    of `dtype`; shorter arrays are refused (the C side cannot see lengths)."""
+    arr = np.ascontiguousarray(a, dtype)
+    if arr.size < count:
+        raise ValueError(f"{what} holds {arr.size} entries; {count} are needed")
+    return arr
+
+
+def _host_out(a, dtype, count: int, what: str) -> np.ndarray:
+    """A caller-supplied host output the C ABI writes `count` entries of: it
+    must already have the element type, be contiguous and be long enough,
+    since a converted copy would not be the caller's array."""
+    if not isinstance(a, np.ndarray) or a.dtype != dtype or not a.flags.c_contiguous or not a.flags.writeable:
+        raise ValueError(f"{what} must be a writeable C-contiguous {np.dtype(dtype).name} array")
+    if a.size < count:
+        raise ValueError(f"{what} holds {a.size} entries; {count} are needed")
+    return a
+
+
 def _int32(a, what: str) -> np.ndarray:
     """`a` as a contiguous int32 array; integer values outside int32 are an
     error instead of wrapping."""
@@ -337,8 +357,8 @@ class DeviceMatrix:
     def spmv_host(self, x: np.ndarray, kernel: int = CSR_SCALAR, lanes: int = 4, block: int = 4,
                   acc: int | None = None, out: np.ndarray | None = None, stream=None) -> np.ndarray:
         acc = self.dtype if acc is None else acc
-        x = np.ascontiguousarray(x, _np_dtype(self.dtype))
-        y = out if out is not None else np.empty(self.m, _np_dtype(acc))
+        x = _host_in(x, _np_dtype(self.dtype), self.n, "x")
+        y = _host_out(out, _np_dtype(acc), self.m, "out") if out is not None else np.empty(self.m, _np_dtype(acc))
         s = C.c_void_p(0) if stream is None else _stream_ptr(stream)
         call("spmvb_spmv_host", self.handle, kernel, lanes, block, _ptr(x), _ptr(y), acc, s)
         return y
@@ -346,7 +366,7 @@ class DeviceMatrix:
     def spmm_host(self, X: np.ndarray, k: int, tile: int = 32, bucketed: bool = False,
                   acc: int | None = None, stream=None) -> np.ndarray:
         acc = self.dtype if acc is None else acc
-        X = np.ascontiguousarray(X, _np_dtype(self.dtype))
+        X = _host_in(X, _np_dtype(self.dtype), self.n * k, "X")
         Y = np.empty((self.m, k), _np_dtype(acc))
         s = C.c_void_p(0) if stream is None else _stream_ptr(stream)
         call("spmvb_spmm_host", self.handle, tile, int(bucketed), k, _ptr(X), _ptr(Y), acc, s)
@@ -390,8 +410,13 @@ class Pipeline:
     def submit(self, x: np.ndarray, y: np.ndarray, kernel: int = CSR_SCALAR, lanes: int = 4, block: int = 4,
                acc: int | None = None):
         acc = self.M.dtype if acc is None else acc
-        assert x.dtype == _np_dtype(self.M.dtype) and x.flags.c_contiguous and x.size >= self.M.n
-        assert y.dtype == _np_dtype(acc) and y.flags.c_contiguous and y.size >= self.M.m
+        # Both arrays are used in place (x read, y written after return), so
+        # they must already have the right type, layout and length.
+        if not isinstance(x, np.ndarray) or x.dtype != _np_dtype(self.M.dtype) or not x.flags.c_contiguous \
+                or x.size < self.M.n:
+            raise ValueError(f"x must be a C-contiguous {np.dtype(_np_dtype(self.M.dtype)).name} array of "
+                             f"at least {self.M.n} entries")
+        _host_out(y, _np_dtype(acc), self.M.m, "y")
         self._keep.append((x, y))  # alive until wait()
         call("spmvb_pipeline_submit", self.handle, kernel, lanes, block, _ptr(x), _ptr(y), acc)
 
@@ -434,7 +459,7 @@ class DistMatrix:
             self.handle = None
 
     def set_x(self, x: np.ndarray, stream=None):
-        x = np.ascontiguousarray(x, _np_dtype(self.dtype))
+        x = _host_in(x, _np_dtype(self.dtype), self.m, "x")
         call("spmvb_dist_set_x", self.handle, _ptr(x), _stream_ptr(stream))
 
     def iterate(self, iters: int, kernel: int = CSR_SCALAR, lanes: int = 4, stream=None):

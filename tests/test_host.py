@@ -89,6 +89,24 @@ def test_short_or_out_of_range_arrays_are_refused_before_the_c_call():
         S.write_csr_cache("/nonexistent/never.csrbin", A)
 
 
+def test_host_buffer_checks():
+    """Host inputs shorter than what the C ABI reads, and outputs of the wrong
+    type, layout or length, are refused by the Python layer."""
+    from spmvbench_b200 import _host_in, _host_out
+    assert _host_in([1, 2, 3], np.float64, 3, "x").dtype == np.float64
+    with pytest.raises(ValueError, match="x holds 2 entries"):
+        _host_in(np.ones(2), np.float64, 3, "x")
+    y = np.empty(4)
+    assert _host_out(y, np.float64, 4, "y") is y
+    for bad in (np.empty(3), np.empty(4, np.float32), np.empty((4, 2))[:, 0], [0.0] * 4):
+        with pytest.raises(ValueError):
+            _host_out(bad, np.float64, 4, "y")
+    ro = np.empty(4)
+    ro.flags.writeable = False
+    with pytest.raises(ValueError):
+        _host_out(ro, np.float64, 4, "y")
+
+
 def test_validation_agrees_with_the_csr_rules_on_random_damage():
     """spmvb_csr_validate accepts exactly the CSRs that satisfy rowptr[0] = 0,
     non-decreasing rowptr, rowptr[m] entries in colind, and every column in
