@@ -27,6 +27,9 @@ namespace detail {
 template <typename T>
 SpmmResult run_spmm(const CsrMatrix<T>& A, const std::vector<T>& B, int k, int tile, bool balanced, int iters,
                     int warmup, std::vector<T>& Y) {
+  if (k < 0 || B.size() < static_cast<size_t>(A.n) * static_cast<size_t>(k))
+    throw std::runtime_error("spmm_csr_tiled: B holds " + std::to_string(B.size()) + " values, n*k = " +
+                             std::to_string(static_cast<size_t>(A.n) * static_cast<size_t>(k < 0 ? 0 : k)));
   int dev = 0;
   check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
   spmvb_context ctx = nullptr;

@@ -123,7 +123,12 @@ class SpmvRunner {
   SpmvRunner(const SpmvRunner&) = delete;
   SpmvRunner& operator=(const SpmvRunner&) = delete;
 
+  // x must hold exactly n values (the reference copies x.size() values into
+  // its n-entry device buffer whatever that size is).
   void set_x(const std::vector<T>& x) {
+    if (x.size() != static_cast<std::size_t>(A_.n))
+      throw std::runtime_error("set_x: x holds " + std::to_string(x.size()) + " values, n = " +
+                               std::to_string(A_.n));
     host_x_ = x;
     if (!x.empty())
       detail::check_cuda(cudaMemcpy(d_x_, x.data(), x.size() * sizeof(T), cudaMemcpyHostToDevice), "set_x");

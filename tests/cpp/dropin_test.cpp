@@ -63,6 +63,16 @@ static CsrMatrix<double> sample() {  // tests/test_formats.cpp:13-19
 static void cpu_tests() {
   // Formats (tests/test_formats.cpp:23-107)
   const auto A = sample();
+  {  // a B shorter than n*k is refused before any device work
+    std::vector<double> B(A.n * 3 - 1), Y;
+    bool threw = false;
+    try {
+      spmm_csr_tiled_f64(A, B, 3, 32, false, 1, 0, Y);
+    } catch (const std::runtime_error&) {
+      threw = true;
+    }
+    EXPECT(threw);
+  }
   const auto ell = csr_to_ell(A);
   EXPECT(ell.max_row_nnz == 4 && ell.padded_nnz == 12 && ell.nnz == 7);
   EXPECT(ell.row_lengths == std::vector<int>({2, 1, 4}));
