@@ -251,6 +251,35 @@ def test_shard_renumbering_round_trip(parts):
 
 
 # ---- generators ---------------------------------------------------------------------
+def test_partition_and_shard_on_random_rowptrs():
+    """partition_rows follows its rule (bounds[g] = lower_bound(rowptr,
+    ceil(g*nnz/parts))) on random and skewed rowptrs with empty rows and more
+    parts than rows, and every shard's renumbered columns map back to the
+    owner's slot layout."""
+    rng = np.random.default_rng(3)
+    for t in range(3000):
+        m, parts = int(rng.integers(0, 30)), int(rng.integers(1, 12))
+        lens = rng.integers(0, 5, m) * (rng.random(m) < 0.7)
+        if m and rng.random() < 0.2:
+            lens[rng.integers(0, m)] = 100
+        rp = np.zeros(m + 1, np.int32)
+        rp[1:] = np.cumsum(lens)
+        nnz = int(rp[-1])
+        b = S.partition_rows(rp, parts)
+        exp = [0] + [int(np.searchsorted(rp, -(-g * nnz // parts), side="left")) for g in range(1, parts)] + [m]
+        assert b.tolist() == [min(max(v, 0), m) for v in exp]
+        if m and t % 10 == 0:
+            ci = rng.integers(0, m, nnz).astype(np.int32)
+            A = S.CsrMatrix(m, m, rp, ci, np.ones(nnz))
+            owner = np.searchsorted(b, np.arange(m), side="right") - 1
+            for r in range(parts):
+                mr, lrp, lci = S.shard_csr(A, b, r)
+                slot = owner * mr + (np.arange(m) - b[owner])
+                s0, s1 = rp[b[r]], rp[b[r + 1]]
+                np.testing.assert_array_equal(lrp, rp[b[r]:b[r + 1] + 1] - s0)
+                np.testing.assert_array_equal(lci, slot[ci[s0:s1]])
+
+
 def test_generators_shapes_and_structure():
     A1 = S.generate(1)
     assert (A1.m, A1.n, A1.nnz) == (100000, 100000, 899980)
