@@ -584,6 +584,20 @@ def _write_csv(name, rows):
     print(f"wrote results/{name}")
 
 
+def _workload_id(text: str) -> int:
+    """A seeded workload by id (1..5) or by name (spmvbench_b200.WORKLOADS)."""
+    names = {v: k for k, v in WORKLOADS.items()}
+    if text in names:
+        return names[text]
+    try:
+        w = int(text)
+    except ValueError:
+        w = 0
+    if w not in WORKLOADS:
+        raise argparse.ArgumentTypeError(f"unknown workload {text!r}: one of 1-5 or {', '.join(names)}")
+    return w
+
+
 def main(argv=None):
     p = argparse.ArgumentParser(prog="python -m spmvbench_b200.driver")
     g = p.add_mutually_exclusive_group(required=True)
@@ -593,7 +607,8 @@ def main(argv=None):
     g.add_argument("--validate", action="store_true")
     g.add_argument("--spmm", action="store_true")
     g.add_argument("--profile", metavar="KERNEL")
-    p.add_argument("--workload", type=int, nargs="+", default=[1, 2, 3, 4])
+    p.add_argument("--workload", type=_workload_id, nargs="+", default=[1, 2, 3, 4],
+                   help="workload ids (1-5) or names (" + ", ".join(WORKLOADS.values()) + ")")
     p.add_argument("--matrix", nargs="+", metavar="FILE",
                    help="Matrix Market (.mtx) or CSR-cache (.csrbin) files instead of the seeded workloads")
     p.add_argument("--all", action="store_true", help="every .mtx file in $SPMVBENCH_DATA (default data/)")

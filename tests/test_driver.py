@@ -33,6 +33,10 @@ def test_stats_runs_without_a_gpu():
     out = run("--stats", "--workload", "1", "4")
     assert out.returncode == 0, out.stderr
     assert "banded_100k_hb4" in out.stdout and "dense_share_of_stored_4x4=1" in out.stdout
+    out = run("--stats", "--workload", "banded_100k_hb4")
+    assert out.returncode == 0 and "=== banded_100k_hb4 ===" in out.stdout, out.stderr
+    out = run("--stats", "--workload", "nine")
+    assert out.returncode != 0 and "unknown workload" in out.stderr
 
 
 def test_stats_on_matrix_files_and_data_dir(tmp_path):
