@@ -110,8 +110,9 @@ def bench_row(matrix, precision, label, lanes, block, t, flops, lo, hi, peak, tr
     """One results/bench.csv row. `t` holds the timing summary of _time
     (median/min/mean/max ms per launch, iters, cold ms). bw_pct_peak follows
     the reference (no-reuse traffic over the peak, in percent); roofline_frac
-    is the compulsory traffic over the peak. No vendor baseline runs on this
-    path, so is_baseline is 0 and speedup / baseline are empty."""
+    is the compulsory traffic over the peak. is_baseline is 0 and speedup /
+    baseline are empty here; _measure_all fills speedup and baseline when the
+    cuSPARSE baseline row runs, and marks that row is_baseline = 1."""
     med = t["median_ms"]
     gbs = (lambda b: b / (med * 1e-3) / 1e9) if med > 0 else (lambda b: 0.0)
     row = {"device": "cuda", "matrix": matrix, "precision": precision, "kernel": label, "is_baseline": 0,
