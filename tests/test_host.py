@@ -89,6 +89,71 @@ def test_short_or_out_of_range_arrays_are_refused_before_the_c_call():
         S.write_csr_cache("/nonexistent/never.csrbin", A)
 
 
+def test_c_abi_returns_errors_on_null_and_bad_arguments():
+    """The boundary's contract: a status code, never a crash or an abort,
+    for null pointers, negative sizes and bad ids on every entry point that
+    runs without a GPU, and on the device entry points' handle checks."""
+    import ctypes as C
+    lib = S.load()
+    rp = np.array([0, 1, 2], np.int32)
+    ci = np.array([0, 1], np.int32)
+    one = np.ones(2)
+    out = C.c_void_p()
+    i32, i64 = C.c_int32(), C.c_int64()
+    st = S._lib.RowStats()
+    calls = [
+        lambda: lib.spmvb_query_gpu(0, None),
+        lambda: lib.spmvb_context_create(0, None),
+        lambda: lib.spmvb_compute_row_stats(None, None, 2, 2, 2, C.byref(st), None, 0),
+        lambda: lib.spmvb_compute_row_stats(rp.ctypes.data, ci.ctypes.data, 2, 2, 2, None, None, 0),
+        lambda: lib.spmvb_compute_row_stats(rp.ctypes.data, ci.ctypes.data, -1, 2, 2, C.byref(st), None, 0),
+        lambda: lib.spmvb_compute_row_stats(rp.ctypes.data, ci.ctypes.data, 2, 2, 2, C.byref(st),
+                                            np.zeros(1, np.int64).ctypes.data, 1),
+        lambda: lib.spmvb_choose_spmv(None, None),
+        lambda: lib.spmvb_choose_spmv_reference(None, None),
+        lambda: lib.spmvb_generate(99, 1, 0, C.byref(i32), C.byref(i32), C.byref(i64), None, None, None),
+        lambda: lib.spmvb_generate(1, 1, 0, None, None, None, None, None, None),
+        lambda: lib.spmvb_generate(1, 1, -5, C.byref(i32), C.byref(i32), C.byref(i64), None, None, None),
+        lambda: lib.spmvb_generate_vector(1, 10, None),
+        lambda: lib.spmvb_generate_vector(1, -10, None),
+        lambda: lib.spmvb_read_matrix_market(None, 0, C.byref(out)),
+        lambda: lib.spmvb_read_matrix_market(b"/nonexistent.mtx", 0, None),
+        lambda: lib.spmvb_csr_cache_write(None, 2, 2, 2, rp.ctypes.data, ci.ctypes.data, one.ctypes.data),
+        lambda: lib.spmvb_csr_cache_write(b"/nonexistent/x.csrbin", 2, 2, 2, None, None, None),
+        lambda: lib.spmvb_csr_cache_read(None, None),
+        lambda: lib.spmvb_host_csr_get(None, None, None, None, None, None, None),
+        lambda: lib.spmvb_partition_rows(None, 2, 2, None),
+        lambda: lib.spmvb_partition_rows(rp.ctypes.data, 2, 0, np.zeros(3, np.int32).ctypes.data),
+        lambda: lib.spmvb_partition_rows(rp.ctypes.data, -1, 2, np.zeros(3, np.int32).ctypes.data),
+        lambda: lib.spmvb_shard_csr(2, rp.ctypes.data, ci.ctypes.data, 2, 5, rp.ctypes.data, C.byref(i32),
+                                    C.byref(i64), None, None),
+        lambda: lib.spmvb_shard_csr(2, rp.ctypes.data, ci.ctypes.data, 2, 0, None, C.byref(i32), C.byref(i64),
+                                    None, None),
+        lambda: lib.spmvb_shard_csr(2, rp.ctypes.data, ci.ctypes.data, 2, 0, np.array([0, 3, 2], np.int32).ctypes.data,
+                                    C.byref(i32), C.byref(i64), None, None),
+        lambda: lib.spmvb_matrix_create_csr(None, 1, 2, 2, 2, rp.ctypes.data, ci.ctypes.data, one.ctypes.data,
+                                            C.byref(out)),
+        lambda: lib.spmvb_spmv(None, 0, 4, 4, None, None, 1, None),
+        lambda: lib.spmvb_spmv_host(None, 0, 4, 4, None, None, 1, None),
+        lambda: lib.spmvb_spmm(None, 32, 0, 4, None, None, 1, None),
+        lambda: lib.spmvb_spmv_merge_noalloc(1, 2, 2, 2, None, None, None, None, None, 1, None),
+        lambda: lib.spmvb_pipeline_create(None, 3, C.byref(out)),
+        lambda: lib.spmvb_pipeline_submit(None, 0, 4, 4, None, None, 1),
+        lambda: lib.spmvb_dist_create(None, 2, 0, None, 1, 2, 2, None, None, None, None, C.byref(out)),
+        lambda: lib.spmvb_context_check(None),
+        lambda: lib.spmvb_selftest_wait_timeout(None),
+        lambda: lib.spmvb_probe_gather_rate(None, 10, 100, None),
+    ]
+    for i, f in enumerate(calls):
+        status = f()
+        assert status != 0, i
+        assert lib.spmvb_last_error(), i
+    for destroy in (lib.spmvb_matrix_destroy, lib.spmvb_pipeline_destroy, lib.spmvb_dist_destroy):
+        assert destroy(None) == 0
+    lib.spmvb_host_csr_free(None)
+    assert lib.spmvb_kernel_name(-1) == b"unknown" and lib.spmvb_status_string(99) == b"unknown status"
+
+
 def test_host_buffer_checks():
     """Host inputs shorter than what the C ABI reads, and outputs of the wrong
     type, layout or length, are refused by the Python layer."""
