@@ -10,6 +10,7 @@
 from __future__ import annotations
 
 import math
+import os
 
 import numpy as np
 import pytest
@@ -193,3 +194,22 @@ def test_reference_gpu_path_loads():
     (oracle/_ref/libspmvref_cuda.so, `make -C oracle ref_cuda`) loads, and its
     gpu_available() answers without aborting where there is no GPU."""
     assert oracle.ref_cuda().refcuda_available() in (0, 1)
+
+
+@pytest.mark.skipif(not (oracle.ref_available() and os.path.exists(
+    os.path.join(os.environ.get("SPMVBENCH_REF", "/root/reference"), "tools", "gen_matrices.py"))),
+    reason="the reference tree or oracle/_ref is absent")
+def test_golden_fixtures_regenerate_identically(tmp_path):
+    """tests/golden/make_golden.py, run again from the reference, writes the
+    committed fixtures array for array."""
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    subprocess.run([sys.executable, os.path.join(here, "golden", "make_golden.py"), "--out", str(tmp_path)],
+                   check=True, capture_output=True, timeout=600)
+    for name in GOLDEN_NAMES:
+        g = np.load(os.path.join(here, "golden", f"{name}.npz"))
+        h = np.load(os.path.join(tmp_path, f"{name}.npz"))
+        assert sorted(g.files) == sorted(h.files), name
+        for k in g.files:
+            np.testing.assert_array_equal(g[k], h[k], err_msg=f"{name}:{k}")
