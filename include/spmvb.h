@@ -227,6 +227,10 @@ spmvb_status spmvb_spmv_host(spmvb_matrix A, spmvb_kernel kernel, int lanes,
  * synchronize the device). The caller owns every array on the device: a
  * valid CSR (rowptr m+1, colind/values nnz, as spmvb_csr_validate checks), x
  * (n entries of dtype) and y (m entries of acc); the current device is used.
+ * Unlike spmvb_spmv it does not inspect the pointers (host memory, another
+ * device's memory or a short array are not caught): only null pointers,
+ * negative sizes and nnz > 0 with n == 0 are refused, so check an untrusted
+ * CSR with spmvb_csr_validate first.
  * Scratch lives in a fixed 1,048,832-byte __device__ array held by every GPU
  * that loads the library until exit, which bounds m + nnz to 117,440,512
  * (65,536 merge tiles of 1,792 items); larger requests fail with

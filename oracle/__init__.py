@@ -54,11 +54,28 @@ def port() -> C.CDLL:
                                           C.POINTER(C.c_int32), C.POINTER(C.c_int64), P, P, P]
         _port.orc_row_stats.argtypes = [P, P, C.c_int32, C.c_int32, C.c_int64, P, P]
         _port.orc_choose_spmv.argtypes = [P, P]
+        _port.orc_generate.argtypes = [C.c_int, C.c_uint64, C.c_int32, C.POINTER(C.c_int32),
+                                       C.POINTER(C.c_int32), C.POINTER(C.c_int64), P, P, P]
+        _port.orc_generate.restype = C.c_int
+        _port.orc_generate_vector.argtypes = [C.c_uint64, C.c_int64, P]
     return _port
 
 
 def ref_available() -> bool:
     return os.path.exists(REF_PATH)
+
+
+def reference_tree():
+    """The SpMVBench source tree the tests may read, or None: $SPMVBENCH_REF,
+    else the tree oracle/Makefile built _ref/libspmvref.so from (recorded in
+    _ref/source_tree), if that directory exists on this machine."""
+    path = os.environ.get("SPMVBENCH_REF")
+    if not path:
+        rec = os.path.join(_HERE, "_ref", "source_tree")
+        if os.path.exists(rec):
+            with open(rec) as f:
+                path = f.read().strip()
+    return path if path and os.path.isdir(path) else None
 
 
 def ref() -> C.CDLL:
@@ -252,6 +269,27 @@ def choose_spmv(stats: dict):
     port().orc_choose_spmv(_p(s), _p(out))
     return {"kernel": int(out[0]), "lanes": int(out[1]), "block_r": int(out[2]), "block_c": int(out[3]),
             "rule": int(out[4])}
+
+
+def generate(which: int, seed: int, scale_rows: int = 0):
+    """Seeded workload `which` (1, 2, 4 or 5) from the oracle's own statement
+    of the generator: (m, n, rowptr, colind, values). Identical to the
+    library's spmvb_generate (tests/test_oracle.py), without loading it."""
+    lib = port()
+    m, n, nnz = C.c_int32(), C.c_int32(), C.c_int64()
+    if lib.orc_generate(which, seed, scale_rows, C.byref(m), C.byref(n), C.byref(nnz), None, None, None) != 0:
+        raise ValueError(f"orc_generate: workload {which} with {scale_rows} rows is not covered")
+    rp = np.zeros(m.value + 1, np.int32)
+    ci = np.zeros(max(nnz.value, 1), np.int32)
+    va = np.zeros(max(nnz.value, 1), np.float64)
+    lib.orc_generate(which, seed, scale_rows, C.byref(m), C.byref(n), C.byref(nnz), _p(rp), _p(ci), _p(va))
+    return m.value, n.value, rp, ci[:nnz.value], va[:nnz.value]
+
+
+def generate_vector(seed: int, n: int) -> np.ndarray:
+    out = np.empty(n, np.float64)
+    port().orc_generate_vector(seed, n, _p(out))
+    return out
 
 
 # ---- the reference itself -------------------------------------------------------

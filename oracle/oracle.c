@@ -340,3 +340,139 @@ double orc_gamma_check_d(int32_t m, const int32_t* rowptr, const int32_t* colind
   }
   return worst;
 }
+
+/* ---- seeded workloads -------------------------------------------------------- */
+/* A second, independent statement of the library's seeded workload generator
+ * (xoshiro256** seeded through splitmix64; one stream per purpose), so that a
+ * CPU timing of the reference (bench.py --impl reference) can build its
+ * matrix without loading the CUDA library. tests/test_oracle.py checks that
+ * both generators give identical rowptr, colind, values and vectors.
+ * Workloads: 1 banded (|i-j| <= 4, diagonal + 10), 2 and 5 uniform (16
+ * distinct sorted columns per row), 4 dense 4x4 blocks (8 distinct block
+ * columns per block row). The power-law workload (3) is not restated. */
+typedef struct { uint64_t s[4]; } OrcRng;
+
+static uint64_t orc_splitmix(uint64_t* x) {
+  uint64_t z = (*x += 0x9e3779b97f4a7c15ull);
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+  return z ^ (z >> 31);
+}
+static void orc_rng_init(OrcRng* r, uint64_t seed, uint64_t stream) {
+  uint64_t x = seed ^ (0x632be59bd9b4e019ull * (stream + 1));
+  for (int i = 0; i < 4; ++i) r->s[i] = orc_splitmix(&x);
+}
+static uint64_t orc_rotl(uint64_t v, int k) { return (v << k) | (v >> (64 - k)); }
+static uint64_t orc_next(OrcRng* r) {
+  uint64_t* s = r->s;
+  const uint64_t out = orc_rotl(s[1] * 5, 7) * 9;
+  const uint64_t t = s[1] << 17;
+  s[2] ^= s[0];
+  s[3] ^= s[1];
+  s[1] ^= s[2];
+  s[0] ^= s[3];
+  s[2] ^= t;
+  s[3] = orc_rotl(s[3], 45);
+  return out;
+}
+/* U(-1,1): a 53-bit uniform in [0,1) times 2, minus 1. */
+static double orc_sym(OrcRng* r) { return (double)(orc_next(r) >> 11) * 0x1.0p-53 * 2.0 - 1.0; }
+/* [0, bound) by the high half of a 64x64-bit product. */
+static uint32_t orc_below(OrcRng* r, uint32_t bound) {
+  return (uint32_t)(((unsigned __int128)orc_next(r) * bound) >> 64);
+}
+/* k <= 64 distinct draws in [0, bound) (bound >= 4k), rejection of repeats,
+ * then sorted ascending. */
+static void orc_distinct_sorted(OrcRng* r, int k, uint32_t bound, int32_t* out) {
+  int have = 0;
+  while (have < k) {
+    const int32_t c = (int32_t)orc_below(r, bound);
+    int dup = 0;
+    for (int i = 0; i < have; ++i) dup |= (out[i] == c);
+    if (!dup) out[have++] = c;
+  }
+  qsort(out, (size_t)k, sizeof(int32_t), cmp_i32);
+}
+
+enum { ORC_COLUMNS = 2, ORC_VALUES = 3, ORC_VECTOR = 5 };
+
+/* Sizes of workload `which` (scale_rows > 0 replaces the default row count);
+ * with non-null arrays, also its entries. Returns 0, or -1 for a workload or
+ * size it does not cover. */
+int orc_generate(int which, uint64_t seed, int32_t scale_rows, int32_t* m_out, int32_t* n_out,
+                 int64_t* nnz_out, int32_t* rowptr, int32_t* colind, double* vals) {
+  int32_t m;
+  int64_t nnz;
+  if (which == 1) {
+    m = scale_rows > 0 ? scale_rows : 100000;
+    nnz = 0;
+    for (int32_t i = 0; i < m; ++i) {
+      const int32_t lo = i - 4 < 0 ? 0 : i - 4, hi = i + 4 > m - 1 ? m - 1 : i + 4;
+      nnz += hi - lo + 1;
+    }
+  } else if (which == 2 || which == 5) {
+    m = scale_rows > 0 ? scale_rows : 1000000;
+    if (m < 64) return -1;
+    nnz = (int64_t)m * 16;
+  } else if (which == 4) {
+    m = scale_rows > 0 ? (scale_rows / 4) * 4 : 500000;
+    if (m < 128) return -1;
+    nnz = (int64_t)m * 32;
+  } else {
+    return -1;
+  }
+  *m_out = m;
+  *n_out = m;
+  *nnz_out = nnz;
+  if (!colind) return 0;
+  OrcRng rc, rv;
+  orc_rng_init(&rc, seed, ORC_COLUMNS);
+  orc_rng_init(&rv, seed, ORC_VALUES);
+  int64_t p = 0;
+  rowptr[0] = 0;
+  if (which == 1) {
+    for (int32_t i = 0; i < m; ++i) {
+      const int32_t lo = i - 4 < 0 ? 0 : i - 4, hi = i + 4 > m - 1 ? m - 1 : i + 4;
+      for (int32_t j = lo; j <= hi; ++j, ++p) {
+        colind[p] = j;
+        vals[p] = orc_sym(&rv) + (j == i ? 10.0 : 0.0);
+      }
+      rowptr[i + 1] = (int32_t)p;
+    }
+  } else if (which == 2 || which == 5) {
+    int32_t cols[16];
+    for (int32_t i = 0; i < m; ++i) {
+      orc_distinct_sorted(&rc, 16, (uint32_t)m, cols);
+      for (int t = 0; t < 16; ++t, ++p) {
+        colind[p] = cols[t];
+        vals[p] = orc_sym(&rv);
+      }
+      rowptr[i + 1] = (int32_t)p;
+    }
+  } else {
+    /* Block row b: 8 block columns, then 128 values drawn as block t, row r,
+     * column c at t*16 + r*4 + c; rows are written block by block. */
+    int32_t cols[8];
+    double blk[128];
+    for (int32_t b = 0; b < m / 4; ++b) {
+      orc_distinct_sorted(&rc, 8, (uint32_t)(m / 4), cols);
+      for (int q = 0; q < 128; ++q) blk[q] = orc_sym(&rv);
+      for (int r = 0; r < 4; ++r) {
+        for (int t = 0; t < 8; ++t)
+          for (int c = 0; c < 4; ++c, ++p) {
+            colind[p] = cols[t] * 4 + c;
+            vals[p] = blk[t * 16 + r * 4 + c];
+          }
+        rowptr[b * 4 + r + 1] = (int32_t)p;
+      }
+    }
+  }
+  return 0;
+}
+
+/* `len` values U(-1,1) from the vector stream of `seed`. */
+void orc_generate_vector(uint64_t seed, int64_t len, double* out) {
+  OrcRng r;
+  orc_rng_init(&r, seed, ORC_VECTOR);
+  for (int64_t i = 0; i < len; ++i) out[i] = orc_sym(&r);
+}

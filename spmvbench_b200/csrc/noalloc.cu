@@ -199,6 +199,9 @@ extern "C" spmvb_status spmvb_spmv_merge_noalloc(spmvb_dtype dtype, int32_t m, i
   if (dtype == SPMVB_F64 && acc == SPMVB_F32)
     return fail(SPMVB_ERR_UNSUPPORTED, "fp64 storage with fp32 accumulation is not instantiated");
   if (m < 0 || n < 0 || nnz < 0 || nnz > INT32_MAX) return fail(SPMVB_ERR_INVALID_ARGUMENT, "bad m, n or nnz");
+  // Every stored entry names a column of x, so entries with no columns
+  // would make the kernel read an empty x.
+  if (nnz > 0 && n == 0) return fail(SPMVB_ERR_INVALID_ARGUMENT, "nnz > 0 with n == 0: no column to index");
   if (m == 0) return SPMVB_OK;
   const int64_t items = static_cast<int64_t>(m) + nnz;
   const int64_t tiles = (items + kNoallocTile - 1) / kNoallocTile;

@@ -137,6 +137,9 @@ def test_c_abi_returns_errors_on_null_and_bad_arguments():
         lambda: lib.spmvb_spmv_host(None, 0, 4, 4, None, None, 1, None),
         lambda: lib.spmvb_spmm(None, 32, 0, 4, None, None, 1, None),
         lambda: lib.spmvb_spmv_merge_noalloc(1, 2, 2, 2, None, None, None, None, None, 1, None),
+        # entries but no columns: refused before any pointer is used
+        lambda: lib.spmvb_spmv_merge_noalloc(1, 2, 0, 2, rp.ctypes.data, ci.ctypes.data, one.ctypes.data,
+                                             one.ctypes.data, one.ctypes.data, 1, None),
         lambda: lib.spmvb_pipeline_create(None, 3, C.byref(out)),
         lambda: lib.spmvb_pipeline_submit(None, 0, 4, 4, None, None, 1),
         lambda: lib.spmvb_dist_create(None, 2, 0, None, 1, 2, 2, None, None, None, None, C.byref(out)),
@@ -152,6 +155,20 @@ def test_c_abi_returns_errors_on_null_and_bad_arguments():
         assert destroy(None) == 0
     lib.spmvb_host_csr_free(None)
     assert lib.spmvb_kernel_name(-1) == b"unknown" and lib.spmvb_status_string(99) == b"unknown status"
+
+
+def test_noalloc_size_limit_boundary():
+    """The no-allocation entry point's fixed scratch holds 65,536 merge tiles
+    of 1,792 items (m + nnz <= 117,440,512). One item past that is refused
+    with SPMVB_ERR_UNSUPPORTED; exactly at it the size check passes and the
+    call goes on to fail on its null pointers (no device is touched)."""
+    lib = S.load()
+    limit = 65536 * 1792
+    m = 1_000_000
+    st = lib.spmvb_spmv_merge_noalloc(S.F64, m, m, limit + 1 - m, None, None, None, None, None, S.F64, None)
+    assert st == 3 and b"no-allocation limit" in lib.spmvb_last_error()
+    st = lib.spmvb_spmv_merge_noalloc(S.F64, m, m, limit - m, None, None, None, None, None, S.F64, None)
+    assert st == 1 and b"null device pointer" in lib.spmvb_last_error()
 
 
 def test_host_buffer_checks():

@@ -196,8 +196,8 @@ def test_reference_gpu_path_loads():
     assert oracle.ref_cuda().refcuda_available() in (0, 1)
 
 
-@pytest.mark.skipif(not (oracle.ref_available() and os.path.exists(
-    os.path.join(os.environ.get("SPMVBENCH_REF", "/root/reference"), "tools", "gen_matrices.py"))),
+@pytest.mark.skipif(not (oracle.ref_available() and oracle.reference_tree() and os.path.exists(
+    os.path.join(oracle.reference_tree(), "tools", "gen_matrices.py"))),
     reason="the reference tree or oracle/_ref is absent")
 def test_golden_fixtures_regenerate_identically(tmp_path):
     """tests/golden/make_golden.py, run again from the reference, writes the
@@ -213,3 +213,28 @@ def test_golden_fixtures_regenerate_identically(tmp_path):
         assert sorted(g.files) == sorted(h.files), name
         for k in g.files:
             np.testing.assert_array_equal(g[k], h[k], err_msg=f"{name}:{k}")
+
+
+@pytest.mark.parametrize("which,rows", [(1, 0), (1, 333), (2, 4096), (4, 8192), (5, 1000)])
+def test_oracle_generator_equals_library_generator(which, rows):
+    """The oracle's own statement of the seeded workloads (used by the CPU
+    timing of the reference, which must not load the CUDA library) gives the
+    library's matrices and vectors bit for bit."""
+    import spmvbench_b200 as S
+    m, n, rp, ci, va = oracle.generate(which, 2024, rows)
+    A = S.generate(which, seed=2024, scale_rows=rows)
+    assert (m, n) == (A.m, A.n)
+    np.testing.assert_array_equal(rp, A.rowptr)
+    np.testing.assert_array_equal(ci, A.colind)
+    np.testing.assert_array_equal(va, A.values)
+    np.testing.assert_array_equal(oracle.generate_vector(999, m), S.generate_vector(999, m))
+
+
+def test_oracle_generator_full_uniform_workload():
+    """The full 1M x 1M, 16-per-row workload the reference arm times: equal to
+    the library's, array for array."""
+    import spmvbench_b200 as S
+    m, n, rp, ci, va = oracle.generate(2, 2024)
+    A = S.generate(2, seed=2024)
+    assert m == n == 1_000_000 and ci.size == 16_000_000
+    assert np.array_equal(rp, A.rowptr) and np.array_equal(ci, A.colind) and np.array_equal(va, A.values)

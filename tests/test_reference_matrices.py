@@ -25,7 +25,7 @@ import pytest
 import oracle
 import spmvbench_b200 as S
 
-REF = os.environ.get("SPMVBENCH_REF", "/root/reference")
+REF = oracle.reference_tree() or ""
 
 pytestmark = pytest.mark.skipif(
     not (oracle.ref_available() and os.path.exists(os.path.join(REF, "tools", "gen_matrices.py"))),
