@@ -427,6 +427,28 @@ spmvb_status spmvb_dist_get_info(spmvb_dist D, int32_t* row_begin,
                                  int32_t* row_end, int32_t* max_rows,
                                  int64_t* local_nnz);
 
+/* Single product y = A x over host buffers, row-sharded: each rank passes its
+ * own rows' slice of x (rows bounds[rank]..bounds[rank+1]-1, host) and gets
+ * its rows of y (host). The slices are all-gathered on the devices over
+ * NVLink (ncclAllGather), so each entry of x crosses PCIe once per job, not
+ * once per GPU. Up to `depth` calls in flight, as in spmvb_pipeline; keep x
+ * unchanged and y unread until the call is waited for. Collective: every
+ * rank submits the same sequence of calls. Pinned, mapped y is written by
+ * the kernel directly (every kernel but the merge path). Runs on the NCCL
+ * exchange (not after spmvb_dist_enable_peer). No reference counterpart (the
+ * reference's SpmvRunner copies the whole x to its one GPU,
+ * src/cuda/spmv_cuda.cu:292-330). */
+typedef struct spmvb_dist_pipeline_st* spmvb_dist_pipeline;
+spmvb_status spmvb_dist_pipeline_create(spmvb_dist D, int depth,
+                                        spmvb_dist_pipeline* out);
+spmvb_status spmvb_dist_pipeline_fork(spmvb_dist_pipeline P, void* stream);
+spmvb_status spmvb_dist_pipeline_submit(spmvb_dist_pipeline P,
+                                        spmvb_kernel kernel, int lanes,
+                                        const void* h_x_local, void* h_y_local);
+spmvb_status spmvb_dist_pipeline_join(spmvb_dist_pipeline P, void* stream);
+spmvb_status spmvb_dist_pipeline_wait(spmvb_dist_pipeline P);
+spmvb_status spmvb_dist_pipeline_destroy(spmvb_dist_pipeline P);
+
 #ifdef __cplusplus
 }
 #endif

@@ -154,6 +154,10 @@ def ref_cuda() -> C.CDLL:
                                         C.c_int, C.c_int, P, C.POINTER(C.c_double)]
         lib.refcuda_spmm_dd.argtypes = [C.c_int32, C.c_int32, C.c_int64, P, P, P, P, C.c_int, C.c_int, C.c_int,
                                         C.c_int, C.c_int, P, C.POINTER(C.c_double)]
+        lib.refcuda_runner_create_dd.argtypes = [C.c_int32, C.c_int32, C.c_int64, P, P, P, P]
+        lib.refcuda_runner_create_dd.restype = P
+        lib.refcuda_runner_run.argtypes = [P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double), P]
+        lib.refcuda_runner_destroy.argtypes = [P]
         _ref_cuda = lib
     return _ref_cuda
 
@@ -185,6 +189,33 @@ def ref_cuda_spmm(m, n, rowptr, colind, vals, B, k, tile=32, balanced=False, ite
     ref_cuda().refcuda_spmm_dd(m, n, int(rp[m]) if m else 0, _p(rp), _p(ci), _p(va), _p(BB), k, tile, int(balanced),
                                iters, warmup, _p(Y), C.byref(ms))
     return Y, ms.value
+
+
+class RefCudaRunner:
+    """The reference's SpmvRunner<double,double> on the current GPU, built
+    once for a matrix (its eager ELL / BCSR uploads) with x loaded."""
+
+    def __init__(self, m, n, rowptr, colind, vals, x):
+        self._keep = [np.ascontiguousarray(rowptr, np.int32), np.ascontiguousarray(colind, np.int32),
+                      np.ascontiguousarray(vals, np.float64), np.ascontiguousarray(x, np.float64)]
+        rp, ci, va, xx = self._keep
+        self.m = m
+        self.h = ref_cuda().refcuda_runner_create_dd(m, n, int(rp[m]) if m else 0, _p(rp), _p(ci), _p(va), _p(xx))
+        if not self.h:
+            raise ValueError("refcuda_runner_create_dd: bad sizes")
+
+    def run(self, kernel, lanes=4, block=4, iters=20, warmup=5, want_y=False):
+        """(median ms of the reference's per-launch timing, y or None)."""
+        ms = C.c_double()
+        y = np.empty(self.m, np.float64) if want_y else None
+        if ref_cuda().refcuda_runner_run(self.h, kernel, lanes, block, iters, warmup, C.byref(ms), _p(y)) != 0:
+            raise ValueError(f"refcuda_runner_run: bad kernel id {kernel}")
+        return ms.value, y
+
+    def close(self):
+        if self.h:
+            ref_cuda().refcuda_runner_destroy(self.h)
+            self.h = None
 
 
 _SUF = {(np.float64, np.float64): "dd", (np.float32, np.float32): "ff", (np.float32, np.float64): "fd"}

@@ -50,6 +50,35 @@ int refcuda_spmv_dd(int32_t m, int32_t n, int64_t nnz, const int32_t* rp, const 
   return 0;
 }
 
+// A reference SpmvRunner<double,double> built once (its eager uploads and
+// conversions, src/cuda/spmv_cuda.cu:233-290) with x loaded, for timing
+// several kernels on one matrix. NULL for a bad size.
+void* refcuda_runner_create_dd(int32_t m, int32_t n, int64_t nnz, const int32_t* rp, const int32_t* ci,
+                               const double* v, const double* x) {
+  if (m < 0 || n < 0 || nnz < 0) return nullptr;
+  const R::CsrMatrix<double> A = make(m, n, nnz, rp, ci, v);
+  auto* runner = new R::SpmvRunner<double, double>(A);
+  runner->set_x(std::vector<double>(x, x + n));
+  return runner;
+}
+
+// SpmvRunner::run(kernel, iters, lanes, block, warmup): the median of its
+// per-launch event pairs; y (m doubles) is copied out when non-null.
+int refcuda_runner_run(void* h, int kernel, int lanes, int block, int iters, int warmup, double* median_ms,
+                       double* y) {
+  if (!h || kernel < 0 || kernel > 5) return 1;
+  auto* runner = static_cast<R::SpmvRunner<double, double>*>(h);
+  const R::SpmvResult r = runner->run(static_cast<R::KernelId>(kernel), iters, lanes, block, warmup);
+  *median_ms = r.median_ms;
+  if (y) {
+    const std::vector<double> out = runner->result();
+    for (size_t i = 0; i < out.size(); ++i) y[i] = out[i];
+  }
+  return 0;
+}
+
+void refcuda_runner_destroy(void* h) { delete static_cast<R::SpmvRunner<double, double>*>(h); }
+
 // Y = A B (row-major, k columns) with the reference's spmm_csr_tiled_f64.
 int refcuda_spmm_dd(int32_t m, int32_t n, int64_t nnz, const int32_t* rp, const int32_t* ci, const double* v,
                     const double* B, int k, int tile, int balanced, int iters, int warmup, double* Y,

@@ -20,7 +20,7 @@ from ._lib import (BCSR, CSR_MERGE, CSR_SCALAR, CSR_VECTOR, CSR_WARP, ELL, F32, 
                    KERNEL_NAMES, SpmvbError, call, load)
 
 __all__ = [
-    "CsrMatrix", "Context", "DeviceMatrix", "DistMatrix", "SpmvbError", "generate",
+    "CsrMatrix", "Context", "DeviceMatrix", "DistMatrix", "DistPipeline", "SpmvbError", "generate",
     "read_matrix_market", "write_csr_cache", "read_csr_cache", "Pipeline",
     "generate_vector", "row_stats", "choose_spmv", "choose_spmv_reference", "partition_rows",
     "launch_count", "gpu_available", "csr_validate", "shard_csr", "query_gpu", "kernel_name", "nccl_unique_id",
@@ -487,8 +487,59 @@ class DistMatrix:
         call("spmvb_dist_get_x", self.handle, _ptr(out), _stream_ptr(stream))
         return out
 
+    def row_range(self) -> tuple[int, int]:
+        i = self.info()
+        return i["row_begin"], i["row_end"]
+
     def info(self) -> dict:
         a, b, c = C.c_int32(), C.c_int32(), C.c_int32()
         d = C.c_int64()
         call("spmvb_dist_get_info", self.handle, C.byref(a), C.byref(b), C.byref(c), C.byref(d))
         return {"row_begin": a.value, "row_end": b.value, "max_rows": c.value, "local_nnz": d.value}
+
+
+class DistPipeline:
+    """Row-sharded y = A x over host buffers (spmvb_dist_pipeline): each rank
+    submits its own rows' slice of x and receives its rows of y; the slices
+    are all-gathered on the devices over NVLink. Collective: every rank makes
+    the same sequence of submits. Keep x unchanged and y unread until wait()
+    (or join())."""
+
+    def __init__(self, D: DistMatrix, depth: int = 3):
+        h = C.c_void_p()
+        call("spmvb_dist_pipeline_create", D.handle, depth, C.byref(h))
+        self.handle = h
+        self.D = D
+        self.rows = D.row_range()[1] - D.row_range()[0]
+        self._keep = []
+
+    def fork(self, stream):
+        call("spmvb_dist_pipeline_fork", self.handle, _stream_ptr(stream))
+
+    def submit(self, x_local: np.ndarray, y_local: np.ndarray, kernel: int = CSR_SCALAR, lanes: int = 4):
+        dt = _np_dtype(self.D.dtype)
+        if not isinstance(x_local, np.ndarray) or x_local.dtype != dt or not x_local.flags.c_contiguous \
+                or x_local.size < self.rows:
+            raise ValueError(f"x_local must be a C-contiguous {np.dtype(dt).name} array of at least "
+                             f"{self.rows} entries")
+        _host_out(y_local, dt, self.rows, "y_local")
+        self._keep.append((x_local, y_local))
+        call("spmvb_dist_pipeline_submit", self.handle, kernel, lanes, _ptr(x_local), _ptr(y_local))
+
+    def join(self, stream):
+        call("spmvb_dist_pipeline_join", self.handle, _stream_ptr(stream))
+
+    def wait(self):
+        call("spmvb_dist_pipeline_wait", self.handle)
+        self._keep.clear()
+
+    def close(self):
+        if getattr(self, "handle", None):
+            load().spmvb_dist_pipeline_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -117,6 +117,12 @@ SIGNATURES = {
     "spmvb_dist_enable_peer": (C.c_int, [P, P]),
     "spmvb_dist_exchange": (C.c_int, [P]),
     "spmvb_dist_get_info": (C.c_int, [P, I32P, I32P, I32P, I64P]),
+    "spmvb_dist_pipeline_create": (C.c_int, [P, C.c_int, C.POINTER(P)]),
+    "spmvb_dist_pipeline_fork": (C.c_int, [P, P]),
+    "spmvb_dist_pipeline_submit": (C.c_int, [P, C.c_int, C.c_int, P, P]),
+    "spmvb_dist_pipeline_join": (C.c_int, [P, P]),
+    "spmvb_dist_pipeline_wait": (C.c_int, [P]),
+    "spmvb_dist_pipeline_destroy": (C.c_int, [P]),
     "spmvb_pipeline_create": (C.c_int, [P, C.c_int, C.POINTER(P)]),
     "spmvb_pipeline_fork": (C.c_int, [P, P]),
     "spmvb_pipeline_submit": (C.c_int, [P, C.c_int, C.c_int, C.c_int, P, P, C.c_int]),

@@ -591,3 +591,138 @@ spmvb_status spmvb_dist_get_info(spmvb_dist D, int32_t* row_begin, int32_t* row_
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Host-buffer product over the row shards: every rank passes its own rows'
+// slice of x (host) and receives its rows of y (host). On the device the
+// slices are all-gathered over NVLink (ncclAllGather, in place into the
+// padded x of the call's slot), so each entry of x crosses PCIe once per job
+// instead of once per GPU. Slots as in spmvb_pipeline (pipeline.cpp): each
+// has its own stream, padded x and staging y; every all-gather runs on one
+// communication stream, in submit order, which is the same on every rank.
+// ---------------------------------------------------------------------------
+struct spmvb_dist_pipeline_st {
+  spmvb_dist D = nullptr;
+  struct Slot {
+    cudaStream_t stream = nullptr;
+    cudaEvent_t copied = nullptr, gathered = nullptr, done = nullptr;
+    DevBuf x, y;
+    bool used = false;
+  };
+  std::vector<Slot> slots;
+  cudaStream_t comm = nullptr;
+  cudaEvent_t fork = nullptr;
+  int next = 0;
+
+  ~spmvb_dist_pipeline_st() {
+    if (comm) cudaStreamSynchronize(comm);
+    for (auto& s : slots) {
+      if (s.stream) cudaStreamSynchronize(s.stream);
+      for (cudaEvent_t e : {s.copied, s.gathered, s.done})
+        if (e) cudaEventDestroy(e);
+      if (s.stream) cudaStreamDestroy(s.stream);
+    }
+    if (comm) cudaStreamDestroy(comm);
+    if (fork) cudaEventDestroy(fork);
+  }
+};
+
+extern "C" {
+
+spmvb_status spmvb_dist_pipeline_create(spmvb_dist D, int depth, spmvb_dist_pipeline* out) {
+  clear_error();
+  if (!D || !out) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null argument");
+  if (depth < 1 || depth > 16) return fail(SPMVB_ERR_INVALID_ARGUMENT, "depth must be in [1, 16]");
+  if (D->peer) return fail(SPMVB_ERR_UNSUPPORTED, "the host-buffer product runs on the NCCL exchange, not after enable_peer");
+  *out = nullptr;
+  DeviceGuard g(D->ctx->device);
+  auto P = std::make_unique<spmvb_dist_pipeline_st>();
+  P->D = D;
+  P->slots.resize(depth);
+  const size_t es = dtype_size(D->dtype);
+  SPMVB_TRY_CUDA(cudaStreamCreateWithFlags(&P->comm, cudaStreamNonBlocking));
+  SPMVB_TRY_CUDA(cudaEventCreateWithFlags(&P->fork, cudaEventDisableTiming));
+  for (auto& s : P->slots) {
+    SPMVB_TRY_CUDA(cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking));
+    for (cudaEvent_t* e : {&s.copied, &s.gathered, &s.done})
+      SPMVB_TRY_CUDA(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
+    SPMVB_TRY(s.x.alloc(size_t(std::max(D->nranks * D->max_rows, 1)) * es));
+    SPMVB_TRY(s.y.alloc(size_t(std::max(D->max_rows, 1)) * es));
+  }
+  *out = P.release();
+  return SPMVB_OK;
+}
+
+spmvb_status spmvb_dist_pipeline_fork(spmvb_dist_pipeline P, void* stream) {
+  clear_error();
+  if (!P) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null pipeline");
+  DeviceGuard g(P->D->ctx->device);
+  SPMVB_TRY_CUDA(cudaEventRecord(P->fork, static_cast<cudaStream_t>(stream)));
+  SPMVB_TRY_CUDA(cudaStreamWaitEvent(P->comm, P->fork, 0));
+  for (auto& s : P->slots) SPMVB_TRY_CUDA(cudaStreamWaitEvent(s.stream, P->fork, 0));
+  return SPMVB_OK;
+}
+
+spmvb_status spmvb_dist_pipeline_submit(spmvb_dist_pipeline P, spmvb_kernel kernel, int lanes,
+                                        const void* h_x_local, void* h_y_local) {
+  clear_error();
+  if (!P) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null pipeline");
+  spmvb_dist D = P->D;
+  const int32_t rows = D->bounds[D->rank + 1] - D->bounds[D->rank];
+  if (rows && (!h_x_local || !h_y_local)) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null host buffer");
+  if (kernel < 0 || kernel >= SPMVB_KERNEL_COUNT) return fail(SPMVB_ERR_INVALID_ARGUMENT, "unknown kernel id");
+  DeviceGuard g(D->ctx->device);
+  SPMVB_TRY(spmvb_matrix_prepare(D->local, kernel, 0));
+  auto& s = P->slots[P->next];
+  P->next = (P->next + 1) % static_cast<int>(P->slots.size());
+  const size_t es = dtype_size(D->dtype);
+  unsigned char* mine = s.x.as<unsigned char>() + size_t(D->rank) * D->max_rows * es;
+  if (rows) SPMVB_TRY_CUDA(cudaMemcpyAsync(mine, h_x_local, size_t(rows) * es, cudaMemcpyHostToDevice, s.stream));
+  if (D->nranks > 1) {
+    const ncclDataType_t t = D->dtype == SPMVB_F64 ? ncclFloat64 : ncclFloat32;
+    SPMVB_TRY_CUDA(cudaEventRecord(s.copied, s.stream));
+    SPMVB_TRY_CUDA(cudaStreamWaitEvent(P->comm, s.copied, 0));
+    SPMVB_TRY(nccl_enqueued(D->comm, ncclAllGather(mine, s.x.get(), size_t(D->max_rows), t, D->comm, P->comm),
+                            "ncclAllGather(x slices)"));
+    SPMVB_TRY_CUDA(cudaEventRecord(s.gathered, P->comm));
+    SPMVB_TRY_CUDA(cudaStreamWaitEvent(s.stream, s.gathered, 0));
+  }
+  void* y_direct = (rows && stores_y_once(kernel)) ? mapped_host_ptr(h_y_local) : nullptr;
+  if (y_direct) {
+    SPMVB_TRY(spmvb_spmv(D->local, kernel, lanes, 4, s.x.get(), y_direct, D->dtype, s.stream));
+  } else {
+    SPMVB_TRY(spmvb_spmv(D->local, kernel, lanes, 4, s.x.get(), s.y.get(), D->dtype, s.stream));
+    if (rows) SPMVB_TRY_CUDA(cudaMemcpyAsync(h_y_local, s.y.get(), size_t(rows) * es, cudaMemcpyDeviceToHost, s.stream));
+  }
+  SPMVB_TRY_CUDA(cudaEventRecord(s.done, s.stream));
+  s.used = true;
+  return SPMVB_OK;
+}
+
+spmvb_status spmvb_dist_pipeline_join(spmvb_dist_pipeline P, void* stream) {
+  clear_error();
+  if (!P) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null pipeline");
+  DeviceGuard g(P->D->ctx->device);
+  for (auto& s : P->slots)
+    if (s.used) SPMVB_TRY_CUDA(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), s.done, 0));
+  return SPMVB_OK;
+}
+
+spmvb_status spmvb_dist_pipeline_wait(spmvb_dist_pipeline P) {
+  clear_error();
+  if (!P) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null pipeline");
+  DeviceGuard g(P->D->ctx->device);
+  SPMVB_TRY_CUDA(cudaStreamSynchronize(P->comm));
+  for (auto& s : P->slots) SPMVB_TRY_CUDA(cudaStreamSynchronize(s.stream));
+  return check_err_word(P->D->ctx, P->slots[0].stream);
+}
+
+spmvb_status spmvb_dist_pipeline_destroy(spmvb_dist_pipeline P) {
+  clear_error();
+  if (!P) return SPMVB_OK;
+  DeviceGuard g(P->D->ctx->device);
+  delete P;
+  return SPMVB_OK;
+}
+
+}  // extern "C"

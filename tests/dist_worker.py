@@ -81,6 +81,32 @@ for which, rows, kernel in ((2, 200000, S.ELL), (3, 300000, S.CSR_MERGE), (1, 0,
         print(f"rank {rank} workload {which} kernel {S.kernel_name(kernel)} exchange {exchange}: "
               f"{'ok' if ok else 'MISMATCH'}", flush=True)
         bad += not ok
+# Host-buffer product over the row blocks (spmvb_dist_pipeline): each rank
+# submits its rows' slice of x and must get its rows of csr_omp's y.
+for which, rows, kernel in ((2, 200000, S.ELL), (3, 300000, S.CSR_MERGE)):
+    A = S.generate(which, seed=95, scale_rows=rows)
+    bounds = S.partition_rows(A.rowptr, world)
+    r0, r1 = int(bounds[rank]), int(bounds[rank + 1])
+    obj = [S.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    D = S.DistMatrix(ctx, world, rank, obj[0], A, bounds, S.F64)
+    P = S.DistPipeline(D, depth=3)
+    xs = [S.generate_vector(96 + i, A.n) for i in range(5)]
+    ys = [torch.empty(max(r1 - r0, 1), dtype=torch.float64).pin_memory() for _ in range(5)]
+    xl = [torch.from_numpy(x[r0:r1].copy()).pin_memory() for x in xs]
+    for i in range(5):
+        P.submit(xl[i].numpy(), ys[i].numpy(), kernel=kernel)
+    P.wait()
+    ok = True
+    for i in range(5):
+        ref = oracle.spmv_csr(A.m, A.rowptr, A.colind, A.values, xs[i], np.float64)[r0:r1]
+        got = ys[i].numpy()[:r1 - r0]
+        ok &= np.allclose(got, ref, rtol=1e-9, atol=1e-12) if kernel == S.CSR_MERGE else np.array_equal(got, ref)
+    P.close()
+    D.close()
+    print(f"rank {rank} workload {which} kernel {S.kernel_name(kernel)} exchange pipeline: "
+          f"{'ok' if ok else 'MISMATCH'}", flush=True)
+    bad += not ok
 dist.barrier()
 dist.destroy_process_group()
 sys.exit(1 if bad else 0)

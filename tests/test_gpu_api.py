@@ -14,7 +14,7 @@ import torch
 
 import oracle
 import spmvbench_b200 as S
-from gpu_util import assert_bitwise, oracle_y, run_spmv
+from gpu_util import assert_bitwise, assert_rows_within_bound, oracle_y, run_spmv
 
 pytestmark = pytest.mark.gpu
 
@@ -104,6 +104,32 @@ def test_single_rank_iteration_matches_oracle(ctx):
     assert_bitwise(x, got, "iterated")
     kms, sms = D.iterate_timed(2, kernel=S.CSR_SCALAR)
     assert 0 < kms <= sms
+    D.close()
+
+
+@pytest.mark.parametrize("depth,kernel", [(1, "ELL"), (3, "ELL"), (3, "CSR_MERGE")])
+def test_dist_pipeline_single_rank_matches_oracle(ctx, depth, kernel):
+    """The row-sharded host-buffer product with one rank: 6 calls with
+    different x (pinned) in flight, each y equal to csr_omp (bit for bit
+    for ELL, through staged y for the merge path within gamma_n)."""
+    k = getattr(S, kernel)
+    A = S.generate(2, seed=84, scale_rows=70000)
+    D = S.DistMatrix(ctx, 1, 0, None, A, S.partition_rows(A.rowptr, 1), S.F64)
+    P = S.DistPipeline(D, depth=depth)
+    xs = [torch.from_numpy(S.generate_vector(85 + i, A.n)).pin_memory() for i in range(6)]
+    ys = [torch.full((A.m,), float("nan"), dtype=torch.float64).pin_memory() for _ in range(6)]
+    for i in range(6):
+        P.submit(xs[i].numpy(), ys[i].numpy(), kernel=k)
+    P.wait()
+    for i in range(6):
+        ref = oracle_y(A, xs[i].numpy(), S.F64, S.F64)
+        if k == S.CSR_MERGE:
+            assert_rows_within_bound(A, xs[i].numpy(), ref, ys[i].numpy(), S.F64, S.F64, f"call {i}")
+        else:
+            assert_bitwise(ref, ys[i].numpy(), f"call {i}")
+    with pytest.raises(ValueError):
+        P.submit(xs[0].numpy()[:10], ys[0].numpy(), kernel=k)
+    P.close()
     D.close()
 
 
