@@ -68,11 +68,11 @@ import sys
 import threading
 import time
 
-# The CPU runs (both arms) bind their OpenMP threads to neighbouring cores; the
-# runtime reads this when it is first loaded.
-os.environ.setdefault("OMP_PROC_BIND", "close")
-
 import numpy as np  # noqa: E402
+
+# Every CPU this process may use, read before any OpenMP runtime starts: a
+# runtime started with OMP_PROC_BIND set binds the calling thread to one CPU.
+HOST_CPUS = sorted(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else None
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
@@ -108,10 +108,17 @@ def bench_config(world: int, kernel: str) -> dict:
 
 
 def host_threads() -> int:
-    try:
-        return len(os.sched_getaffinity(0))
-    except AttributeError:
-        return os.cpu_count() or 1
+    return len(HOST_CPUS) if HOST_CPUS else (os.cpu_count() or 1)
+
+
+def prepare_cpu_run():
+    """Before the oracle's OpenMP runtime first loads: all host CPUs back in
+    this thread's mask (torch's own runtime may have narrowed it) and the
+    threads bound to neighbouring cores (OMP_PROC_BIND=close, read when the
+    runtime starts)."""
+    if HOST_CPUS:
+        os.sched_setaffinity(0, HOST_CPUS)
+    os.environ["OMP_PROC_BIND"] = "close"
 
 
 def spmv_bytes(m, n, nnz, vbytes=8, ibytes=4, ybytes=8):
@@ -242,6 +249,7 @@ def run_reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    prepare_cpu_run()
     import oracle
     m, n, rp, ci, va = oracle.generate(2, SEED)
     x = oracle.generate_vector(X_SEED, n)
@@ -755,6 +763,7 @@ def main():
             workloads = workload_sweep(torch, S, ctx, stream, A, peak, flush, log)
             del flush
         if not args.no_cpu_baseline:
+            prepare_cpu_run()
             run, kind = csr_omp_runner(A.m, A.n, A.rowptr, A.colind, A.values, xh, host_threads())
             cms, cmean, runs = time_csr_omp(run, 3, budget_s=10.0)
             cpu = {"value": 2.0 * A.nnz / (cms * 1e-3) / 1e9, "unit": "GFLOP/s", "cores": host_threads(),

@@ -276,6 +276,13 @@ spmvb_status spmvb_compute_row_stats(const int32_t* h_rowptr, const int32_t* h_c
                              int32_t m, int32_t n, int64_t nnz,
                              spmvb_row_stats* out, int64_t* h_histogram,
                              int64_t hist_cap);
+/* The same statistics, bit for bit, of a matrix already on the device: the
+ * 4x4 block census (the O(nnz) part, src/stats.cpp:85-118 in the reference,
+ * O(L^2) per block row there) runs on the GPU as one radix sort of block
+ * keys; lengths, median and variance come from the handle's host rowptr in
+ * the reference's order. Replaces compute_row_stats for uploaded matrices. */
+spmvb_status spmvb_matrix_row_stats(spmvb_matrix A, spmvb_row_stats* out,
+                                    int64_t* h_histogram, int64_t hist_cap);
 /* Replaces choose_spmv (include/spmvbench/select.hpp:33) with rules
  * calibrated on B200 measurements. */
 spmvb_status spmvb_choose_spmv(const spmvb_row_stats* stats,

@@ -335,6 +335,17 @@ class DeviceMatrix:
     def prepare(self, kernel: int, param: int = 0) -> None:
         call("spmvb_matrix_prepare", self.handle, kernel, param)
 
+    def row_stats(self, histogram: bool = False) -> dict:
+        """row_stats() of the uploaded matrix, with the block census on the
+        device (spmvb_matrix_row_stats); bit-identical to row_stats(A)."""
+        s = _lib.RowStats()
+        hist = np.zeros(self.info()["max_row_nnz"] + 1, np.int64) if histogram else None
+        call("spmvb_matrix_row_stats", self.handle, C.byref(s), _ptr(hist), 0 if hist is None else hist.size)
+        d = {f: getattr(s, f) for f, _ in _lib.RowStats._fields_}
+        if histogram:
+            d["row_nnz_histogram"] = hist
+        return d
+
     def info(self) -> dict:
         i = _lib.MatrixInfo()
         call("spmvb_matrix_get_info", self.handle, C.byref(i))

@@ -99,6 +99,7 @@ SIGNATURES = {
     "spmvb_probe_gather_rate": (C.c_int, [P, C.c_int64, C.c_int64, C.POINTER(C.c_double)]),
     "spmvb_compute_row_stats": (C.c_int, [P, P, C.c_int32, C.c_int32, C.c_int64,
                                           C.POINTER(RowStats), P, C.c_int64]),
+    "spmvb_matrix_row_stats": (C.c_int, [P, C.POINTER(RowStats), P, C.c_int64]),
     "spmvb_choose_spmv": (C.c_int, [C.POINTER(RowStats), C.POINTER(Choice)]),
     "spmvb_choose_spmv_reference": (C.c_int, [C.POINTER(RowStats), C.POINTER(Choice)]),
     "spmvb_kernel_name": (C.c_char_p, [C.c_int]),

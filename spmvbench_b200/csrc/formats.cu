@@ -8,8 +8,9 @@
 //  BCSR  - layout of csr_to_bcsr<T,R,C> (src/formats.cpp:45-105): blocks of a
 //          block row in ascending block-column order, R*C row-major values,
 //          zero fill, and for repeated (row, column) entries the last one in
-//          CSR order wins. Built on the host with a per-block-row sort
-//          (O(L log L) instead of the reference's O(L^2) search) and uploaded.
+//          CSR order wins. Built on the device by one stable radix sort of
+//          the entries' (block, slot) keys (convert.cu) instead of the
+//          reference's O(L^2) host search.
 //  merge - merge-path tile start rows (device binary search) and the carry
 //          scratch of the merge kernel.
 //  buckets - SpMM row ids grouped by length (<= 8, <= 64, > 64), each group
@@ -250,74 +251,17 @@ spmvb_status build_hyb(spmvb_matrix A, int forced_k) {
   return SPMVB_OK;
 }
 
-// Host CSR -> BCSR with the reference's layout rules.
-template <typename V>
-static void csr_to_bcsr_host(const spmvb_matrix A, int R, int C, std::vector<int32_t>& browptr,
-                             std::vector<int32_t>& bcol, std::vector<V>& bval) {
-  const int m = A->m;
-  const int mb = (m + R - 1) / R;
-  const V* vals = reinterpret_cast<const V*>(A->h_values.data());
-  browptr.assign(static_cast<size_t>(mb) + 1, 0);
-  bcol.clear();
-  bval.clear();
-  struct Ent {
-    int32_t bj;
-    int32_t slot;  // r*C + cc
-    int64_t p;
-  };
-  std::vector<Ent> ents;
-  for (int bi = 0; bi < mb; ++bi) {
-    ents.clear();
-    for (int r = 0; r < R; ++r) {
-      const int i = bi * R + r;
-      if (i >= m) break;
-      for (int32_t p = A->h_rowptr[i]; p < A->h_rowptr[i + 1]; ++p) {
-        const int32_t col = A->h_colind[p];
-        ents.push_back({col / C, r * C + col % C, p});
-      }
-    }
-    // Ascending block column; within a block the CSR order (r, then p) is
-    // kept, so the last write of a repeated (row, column) wins.
-    std::stable_sort(ents.begin(), ents.end(), [](const Ent& a, const Ent& b) { return a.bj < b.bj; });
-    size_t a = 0;
-    while (a < ents.size()) {
-      size_t b = a;
-      const size_t base = bval.size();
-      bval.resize(base + static_cast<size_t>(R) * C, V(0));
-      bcol.push_back(ents[a].bj);
-      while (b < ents.size() && ents[b].bj == ents[a].bj) {
-        bval[base + ents[b].slot] = vals[ents[b].p];
-        ++b;
-      }
-      a = b;
-    }
-    browptr[bi + 1] = static_cast<int32_t>(bcol.size());
-  }
-}
-
 spmvb_status build_bcsr(spmvb_matrix A, int block) {
   std::lock_guard<std::mutex> lk(A->build_mu);
   auto& B = block == 2 ? A->bcsr2 : A->bcsr4;
   if (B.built) return SPMVB_OK;
   DeviceGuard g(A->device);
-  std::vector<int32_t> browptr, bcol;
+  // Worst case every entry is its own block; the sort needs keys, entry
+  // indices, block numbers and their double buffers beside it.
   const size_t es = dtype_size(A->dtype);
-  std::vector<unsigned char> bytes;
-  if (es == 8) {
-    std::vector<double> v;
-    csr_to_bcsr_host<double>(A, block, block, browptr, bcol, v);
-    bytes.assign(reinterpret_cast<unsigned char*>(v.data()), reinterpret_cast<unsigned char*>(v.data() + v.size()));
-  } else {
-    std::vector<float> v;
-    csr_to_bcsr_host<float>(A, block, block, browptr, bcol, v);
-    bytes.assign(reinterpret_cast<unsigned char*>(v.data()), reinterpret_cast<unsigned char*>(v.data() + v.size()));
-  }
-  SPMVB_TRY(check_fits(A, static_cast<double>(bytes.size() + bcol.size() * 4 + browptr.size() * 4), "BCSR"));
-  SPMVB_TRY(upload(B.rowptr, browptr.data(), browptr.size() * 4, browptr.size() * 4));
-  SPMVB_TRY(upload(B.colind, bcol.data(), bcol.size() * 4, (bcol.size() + kPad) * 4));
-  SPMVB_TRY(upload(B.values, bytes.data(), bytes.size(), bytes.size() + kPad * es));
-  B.mb = static_cast<int>(browptr.size()) - 1;
-  B.block_nnz = static_cast<int64_t>(bcol.size());
+  const double rc = static_cast<double>(block) * block;
+  SPMVB_TRY(check_fits(A, static_cast<double>(A->nnz) * (rc * es + 4 + 40) + 4.0 * A->m, "BCSR"));
+  SPMVB_TRY(convert_bcsr_device(A, block));
   B.built = true;
   return SPMVB_OK;
 }

@@ -5,7 +5,9 @@
 // possible 4x4 blocks holding more than 8 stored entries (duplicates counted,
 // as the reference counts them). The dense-block count sorts each block row's
 // block columns instead of the reference's linear search (O(L log L) instead
-// of O(L^2) per block row); the counts are identical.
+// of O(L^2) per block row); the counts are identical. spmvb_matrix_row_stats
+// takes the census from the device (one radix sort of block keys,
+// convert.cu) and the rest from the handle's host rowptr, in the same order.
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
@@ -15,14 +17,12 @@
 
 using namespace spmvb;
 
-extern "C" spmvb_status spmvb_compute_row_stats(const int32_t* h_rowptr, const int32_t* h_colind,
-                                        int32_t m, int32_t n, int64_t nnz,
-                                        spmvb_row_stats* out, int64_t* h_histogram,
-                                        int64_t hist_cap) {
-  clear_error();
-  if (!out) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null output");
-  if (m < 0 || n < 0 || nnz < 0) return fail(SPMVB_ERR_INVALID_ARGUMENT, "negative size");
-  if (m > 0 && !h_rowptr) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null rowptr");
+namespace {
+
+// Everything but the 4x4 block census, from rowptr: the reference's
+// accumulation order (lengths in row order, variance summed in row order).
+spmvb_status length_stats(const int32_t* h_rowptr, int32_t m, int32_t n, int64_t nnz, spmvb_row_stats* out,
+                          int64_t* h_histogram, int64_t hist_cap) {
   spmvb_row_stats s{};
   s.nnz = nnz;
   s.rows = m;
@@ -71,10 +71,35 @@ extern "C" spmvb_status spmvb_compute_row_stats(const int32_t* h_rowptr, const i
     for (int i = 0; i < m; ++i) h_histogram[row_nnz[i]]++;
   }
   s.ell_padding_overhead = (nnz > 0) ? static_cast<double>(m) * mx / static_cast<double>(nnz) : 1.0;
+  *out = s;
+  return SPMVB_OK;
+}
 
+void census_fields(spmvb_row_stats* s, int32_t m, int32_t n, int64_t dense_blocks, int64_t stored_blocks) {
+  const int64_t possible = static_cast<int64_t>((m + 3) / 4) * ((n + 3) / 4);
+  s->frac_dense_blocks_4x4 = (possible > 0) ? static_cast<double>(dense_blocks) / possible : 0.0;
+  s->dense_share_of_stored_4x4 =
+      (stored_blocks > 0) ? static_cast<double>(dense_blocks) / static_cast<double>(stored_blocks) : 0.0;
+}
+
+}  // namespace
+
+extern "C" spmvb_status spmvb_compute_row_stats(const int32_t* h_rowptr, const int32_t* h_colind,
+                                        int32_t m, int32_t n, int64_t nnz,
+                                        spmvb_row_stats* out, int64_t* h_histogram,
+                                        int64_t hist_cap) {
+  clear_error();
+  if (!out) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null output");
+  if (m < 0 || n < 0 || nnz < 0) return fail(SPMVB_ERR_INVALID_ARGUMENT, "negative size");
+  if (m > 0 && !h_rowptr) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null rowptr");
+  spmvb_row_stats s{};
+  SPMVB_TRY(length_stats(h_rowptr, m, n, nnz, &s, h_histogram, hist_cap));
+  if (m <= 0) {
+    *out = s;
+    return SPMVB_OK;
+  }
   const int R = 4, C = 4;
   const int mb = (m + R - 1) / R;
-  const int nb = (n + C - 1) / C;
   int64_t dense_blocks = 0, stored_blocks = 0;
   if (h_colind != nullptr && nnz > 0) {
     std::vector<int32_t> bcols;
@@ -95,10 +120,23 @@ extern "C" spmvb_status spmvb_compute_row_stats(const int32_t* h_rowptr, const i
       }
     }
   }
-  const int64_t possible = static_cast<int64_t>(mb) * nb;
-  s.frac_dense_blocks_4x4 = (possible > 0) ? static_cast<double>(dense_blocks) / possible : 0.0;
-  s.dense_share_of_stored_4x4 =
-      (stored_blocks > 0) ? static_cast<double>(dense_blocks) / static_cast<double>(stored_blocks) : 0.0;
+  census_fields(&s, m, n, dense_blocks, stored_blocks);
+  *out = s;
+  return SPMVB_OK;
+}
+
+extern "C" spmvb_status spmvb_matrix_row_stats(spmvb_matrix A, spmvb_row_stats* out, int64_t* h_histogram,
+                                               int64_t hist_cap) {
+  clear_error();
+  if (!A || !out) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null argument");
+  DeviceGuard g(A->device);
+  spmvb_row_stats s{};
+  SPMVB_TRY(length_stats(A->h_rowptr.data(), A->m, A->n, A->nnz, &s, h_histogram, hist_cap));
+  if (A->m > 0) {
+    int64_t dense_blocks = 0, stored_blocks = 0;
+    SPMVB_TRY(block_census_device(A, &dense_blocks, &stored_blocks));
+    census_fields(&s, A->m, A->n, dense_blocks, stored_blocks);
+  }
   *out = s;
   return SPMVB_OK;
 }

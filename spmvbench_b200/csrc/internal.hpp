@@ -184,6 +184,12 @@ spmvb_status build_bcsr(spmvb_matrix A, int block);
 spmvb_status build_merge(spmvb_matrix A);
 spmvb_status build_buckets(spmvb_matrix A);
 
+// On-device conversions (convert.cu): BCSR block x block (2 or 4) from the
+// uploaded CSR into A->bcsr2 / A->bcsr4, and the 4x4 block census of
+// compute_row_stats (blocks with more than 8 stored entries, blocks with any).
+spmvb_status convert_bcsr_device(spmvb_matrix A, int block);
+spmvb_status block_census_device(spmvb_matrix A, int64_t* dense, int64_t* stored);
+
 // Merge-path tile shape shared by the partition builder and the kernel.
 constexpr int kMergeThreads = 128;
 constexpr int kMergeIpt = 11;

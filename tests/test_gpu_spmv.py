@@ -284,3 +284,61 @@ def test_bcsr_long_block_rows_and_empty_chunks(ctx, dtype, acc):
         M = S.DeviceMatrix(ctx, A, dtype)
         for block in (2, 4):
             check_variant(ctx, A, x, dtype, acc, S.BCSR, 1, block, "bcsr", label, M)
+
+
+def _adversarial_csr(rng):
+    """Small CSR with empty rows, repeated and unsorted columns, dense rows and
+    ragged 2x2 / 4x4 tails (the shapes of tests/test_random_parity.py)."""
+    m = int(rng.integers(1, 60))
+    n = int(rng.integers(1, 70))
+    kind = rng.integers(0, 4)
+    if kind == 0:
+        lens = rng.integers(0, min(n, 6) + 1, m)
+    elif kind == 1:
+        lens = np.where(rng.random(m) < 0.1, rng.integers(0, 3 * n + 1, m), rng.integers(0, 3, m))
+    elif kind == 2:
+        lens = np.full(m, n)
+    else:
+        lens = np.where(rng.random(m) < 0.6, 0, rng.integers(1, n + 1, m))
+    rowptr = np.zeros(m + 1, np.int32)
+    rowptr[1:] = np.cumsum(lens)
+    nnz = int(rowptr[-1])
+    colind = rng.integers(0, n, nnz).astype(np.int32)
+    return S.CsrMatrix(m, n, rowptr, colind, rng.uniform(-1, 1, nnz))
+
+
+def test_device_bcsr_and_row_stats_on_adversarial_matrices(ctx):
+    """The on-device BCSR conversion (one stable radix sort of block keys) and
+    the device block census of row statistics on 120 adversarial matrices:
+    BCSR 2x2 / 4x4 equal the oracle's csr_to_bcsr (the reference's layout,
+    last duplicate wins) bit for bit, and every statistic equals the host
+    computation bit for bit."""
+    rng = np.random.default_rng(77)
+    for t in range(120):
+        A = _adversarial_csr(rng)
+        M = S.DeviceMatrix(ctx, A, S.F64 if t % 2 == 0 else S.F32)
+        vals = A.values if t % 2 == 0 else A.values.astype(np.float32)
+        for b in (2, 4):
+            rp, ci, va = M.export_bcsr(b)
+            orp, oci, ova = oracle.csr_to_bcsr(A.m, A.n, b, A.rowptr, A.colind, vals)
+            assert_bitwise(orp, rp, f"case {t} bcsr{b} rowptr")
+            assert_bitwise(oci, ci, f"case {t} bcsr{b} colind")
+            assert_bitwise(ova, va, f"case {t} bcsr{b} values")
+        host, dev = S.row_stats(A, histogram=True), M.row_stats(histogram=True)
+        for f in host:
+            if f == "row_nnz_histogram":
+                assert_bitwise(host[f], dev[f], f"case {t} histogram")
+            else:
+                assert host[f] == dev[f], (t, f, host[f], dev[f])
+        M.close()
+
+
+@pytest.mark.parametrize("which", [1, 2, 3, 4])
+def test_device_row_stats_equal_host_on_workloads(ctx, which):
+    """Full-size benchmark matrices: the device block census gives the host's
+    statistics bit for bit (and the reference's, through the host pins)."""
+    A = S.generate(which, seed=2024)
+    M = S.DeviceMatrix(ctx, A, S.F64)
+    host, dev = S.row_stats(A), M.row_stats()
+    assert host == dev
+    M.close()
