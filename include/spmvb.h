@@ -408,6 +408,19 @@ spmvb_status spmvb_dist_iterate_timed(spmvb_dist D, spmvb_kernel kernel,
                                       int lanes, int iters, void* stream,
                                       double* kernel_ms, double* step_ms);
 spmvb_status spmvb_dist_get_x(spmvb_dist D, void* h_x, void* stream);
+/* Power iteration on the row-sharded matrix: `iters` steps of
+ *   x <- A x (kernel, then the exchange of the slices), lambda = ||x||_2,
+ *   x <- x / lambda,
+ * with the norm taken by every rank over the whole vector it now holds, in a
+ * fixed order that does not depend on the number of ranks (so every rank,
+ * and a one-rank run, gets the same bits when the kernel keeps csr_omp's
+ * order). *h_lambda receives the last step's norm (an estimate of the
+ * dominant eigenvalue's magnitude); synchronizes. Collective, like
+ * spmvb_dist_iterate; works on either exchange. No reference counterpart
+ * (the reference has no solver loop). */
+spmvb_status spmvb_dist_power_iterate(spmvb_dist D, spmvb_kernel kernel,
+                                      int lanes, int iters, double* h_lambda,
+                                      void* stream);
 
 /* Exchange of x slices between the steps of spmvb_dist_iterate. */
 typedef enum {

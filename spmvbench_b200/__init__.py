@@ -483,6 +483,13 @@ class DistMatrix:
              C.byref(k), C.byref(s))
         return k.value, s.value
 
+    def power_iterate(self, iters: int, kernel: int = CSR_SCALAR, lanes: int = 4, stream=None) -> float:
+        """`iters` steps of x <- A x / ||A x||_2 (collective); returns the last
+        norm, the dominant eigenvalue's magnitude once converged."""
+        lam = C.c_double()
+        call("spmvb_dist_power_iterate", self.handle, kernel, lanes, iters, C.byref(lam), _stream_ptr(stream))
+        return lam.value
+
     def enable_peer(self, stream=None):
         """Collective: switch the x exchange from ncclAllGather to direct
         stores into every rank's x over peer memory (raises SpmvbError with

@@ -115,6 +115,7 @@ SIGNATURES = {
     "spmvb_dist_iterate_timed": (C.c_int, [P, C.c_int, C.c_int, C.c_int, P,
                                            C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "spmvb_dist_get_x": (C.c_int, [P, P, P]),
+    "spmvb_dist_power_iterate": (C.c_int, [P, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_double), P]),
     "spmvb_dist_enable_peer": (C.c_int, [P, P]),
     "spmvb_dist_exchange": (C.c_int, [P]),
     "spmvb_dist_get_info": (C.c_int, [P, I32P, I32P, I32P, I64P]),

@@ -48,6 +48,8 @@ struct spmvb_dist_st {
   int32_t max_rows = 0;
   spmvb_matrix local = nullptr;
   DevBuf x_pad, y_loc;
+  DevBuf bounds_dev;   // bounds on the device (power iteration's norm)
+  DevBuf norm_work;    // norm partials, then the norm itself
 
   // Peer exchange state.
   bool peer = false;
@@ -59,7 +61,8 @@ struct spmvb_dist_st {
   int cur = 0;
   unsigned long long timeout_ns = 0;
   // Captured pairs of peer steps (x parity returns to where it started),
-  // keyed by kernel, lanes and starting parity.
+  // keyed by kernel, lanes and starting parity; and captured single NCCL
+  // steps (parity -1).
   struct Graph {
     int kernel, lanes, parity;
     cudaGraphExec_t exec;
@@ -278,6 +281,9 @@ spmvb_status spmvb_dist_destroy(spmvb_dist D) {
     D->close_peers();
     if (!quiet) (void)D->pmem.release();
   }
+  // Graphs that hold NCCL calls go before the communicator does.
+  for (auto& gr : D->graphs) cudaGraphExecDestroy(gr.exec);
+  D->graphs.clear();
   if (D->comm) {
     ncclCommFinalize(D->comm);
     nccl_wait(D->comm, 30.0, "ncclCommFinalize");
@@ -463,6 +469,41 @@ static spmvb_status peer_graph(spmvb_dist D, spmvb_kernel kernel, int lanes, cud
   return SPMVB_OK;
 }
 
+static spmvb_status dist_step(spmvb_dist D, spmvb_kernel kernel, int lanes, cudaStream_t s);
+
+// The graph of one NCCL-exchange step (SpMV, then the all-gather into x),
+// captured on a private stream on first use (the caller ran one eager step,
+// so formats and NCCL connections exist). Keyed with parity -1.
+static spmvb_status nccl_graph(spmvb_dist D, spmvb_kernel kernel, int lanes, cudaGraphExec_t* exec, uint64_t* kernels) {
+  for (const auto& g : D->graphs)
+    if (g.kernel == kernel && g.lanes == lanes && g.parity == -1) {
+      *exec = g.exec;
+      *kernels = g.kernels;
+      return SPMVB_OK;
+    }
+  if (!D->capture) SPMVB_TRY_CUDA(cudaStreamCreateWithFlags(&D->capture, cudaStreamNonBlocking));
+  const uint64_t before = spmvb_launch_count();
+  SPMVB_TRY_CUDA(cudaStreamBeginCapture(D->capture, cudaStreamCaptureModeRelaxed));
+  const spmvb_status st = dist_step(D, kernel, lanes, D->capture);
+  cudaGraph_t graph = nullptr;
+  const cudaError_t e = cudaStreamEndCapture(D->capture, &graph);
+  const uint64_t captured = spmvb_launch_count() - before;
+  uncount_launch(captured);
+  if (st != SPMVB_OK || e != cudaSuccess) {
+    if (graph) cudaGraphDestroy(graph);
+    cudaGetLastError();
+    return st != SPMVB_OK ? st : cuda_fail(e, "cudaStreamEndCapture");
+  }
+  cudaGraphExec_t ex = nullptr;
+  const cudaError_t ei = cudaGraphInstantiate(&ex, graph, 0);
+  cudaGraphDestroy(graph);
+  if (ei != cudaSuccess) return cuda_fail(ei, "cudaGraphInstantiate");
+  D->graphs.push_back({static_cast<int>(kernel), lanes, -1, ex, captured});
+  *exec = ex;
+  *kernels = captured;
+  return SPMVB_OK;
+}
+
 static spmvb_status dist_step(spmvb_dist D, spmvb_kernel kernel, int lanes, cudaStream_t s) {
   SPMVB_TRY(spmvb_spmv(D->local, kernel, lanes, 4, D->x_pad.get(), D->y_loc.get(), D->dtype, s));
   if (D->nranks > 1) {
@@ -501,7 +542,21 @@ spmvb_status spmvb_dist_iterate(spmvb_dist D, spmvb_kernel kernel, int lanes, in
     for (; left > 0; --left) SPMVB_TRY(peer_step(D, kernel, lanes, s, nullptr));
     return SPMVB_OK;
   }
-  for (int it = 0; it < iters; ++it) SPMVB_TRY(dist_step(D, kernel, lanes, s));
+  // NCCL exchange: from two steps on, one eager step, then replays of the
+  // captured step (no host enqueue work between steps).
+  int left = iters;
+  if (left >= 2 && graphs_enabled()) {
+    SPMVB_TRY(dist_step(D, kernel, lanes, s));
+    --left;
+    cudaGraphExec_t ex = nullptr;
+    uint64_t nk = 0;
+    SPMVB_TRY(nccl_graph(D, kernel, lanes, &ex, &nk));
+    for (; left > 0; --left) {
+      SPMVB_TRY_CUDA(cudaGraphLaunch(ex, s));
+      count_launch(nk);
+    }
+  }
+  for (; left > 0; --left) SPMVB_TRY(dist_step(D, kernel, lanes, s));
   return SPMVB_OK;
 }
 
@@ -576,6 +631,41 @@ spmvb_status spmvb_dist_get_x(spmvb_dist D, void* h_x, void* stream) {
     const int32_t b = D->bounds[r], cnt = D->bounds[r + 1] - b;
     std::memcpy(static_cast<unsigned char*>(h_x) + size_t(b) * es, pad.data() + size_t(r) * D->max_rows * es, size_t(cnt) * es);
   }
+  return SPMVB_OK;
+}
+
+spmvb_status spmvb_dist_power_iterate(spmvb_dist D, spmvb_kernel kernel, int lanes, int iters, double* h_lambda,
+                                      void* stream) {
+  clear_error();
+  if (!D || iters < 1 || !h_lambda) return fail(SPMVB_ERR_INVALID_ARGUMENT, "bad argument");
+  if (D->broken) return fail(SPMVB_ERR_TIMEOUT, "an earlier peer wait gave up; recreate the handle");
+  DeviceGuard g(D->ctx->device);
+  auto s = static_cast<cudaStream_t>(stream);
+  const int parts = norm_blocks(D->m);
+  if (!D->bounds_dev.get()) {
+    SPMVB_TRY(upload(D->bounds_dev, D->bounds.data(), D->bounds.size() * 4, D->bounds.size() * 4));
+    SPMVB_TRY(D->norm_work.alloc(size_t(parts + 1) * 8));
+  }
+  double* partials = D->norm_work.as<double>();
+  double* norm = partials + parts;
+  for (int it = 0; it < iters; ++it) {
+    void* x;
+    if (D->peer) {
+      SPMVB_TRY(peer_step(D, kernel, lanes, s, nullptr));
+      x = x_buf(D, D->cur);
+    } else {
+      SPMVB_TRY(dist_step(D, kernel, lanes, s));
+      x = D->x_pad.get();
+    }
+    // Every rank now holds the whole product: each takes its norm (same
+    // bits everywhere) and scales its own copy, so no other collective runs.
+    // Peers store only into the other x buffer, never into this one.
+    SPMVB_TRY(launch_norm_and_scale(D->dtype, x, D->m, D->bounds_dev.as<int>(), D->nranks, D->max_rows, partials,
+                                    norm, D->ctx->sm_count, s));
+  }
+  SPMVB_TRY_CUDA(cudaMemcpyAsync(h_lambda, norm, 8, cudaMemcpyDeviceToHost, s));
+  SPMVB_TRY_CUDA(cudaStreamSynchronize(s));
+  if (D->peer) SPMVB_TRY(peer_check(D, s));
   return SPMVB_OK;
 }
 

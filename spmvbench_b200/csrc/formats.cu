@@ -16,11 +16,14 @@
 //  buckets - SpMM row ids grouped by length (<= 8, <= 64, > 64), each group
 //          ascending, built on the host from rowptr.
 #include <algorithm>
+#include <cstdlib>
 #include <climits>
 #include <cstring>
 #include <numeric>
 #include <string>
 #include <vector>
+
+#include <cudaTypedefs.h>
 
 #include "internal.hpp"
 #include "spmv_kernels.cuh"
@@ -263,6 +266,57 @@ spmvb_status build_bcsr(spmvb_matrix A, int block) {
   SPMVB_TRY(check_fits(A, static_cast<double>(A->nnz) * (rc * es + 4 + 40) + 4.0 * A->m, "BCSR"));
   SPMVB_TRY(convert_bcsr_device(A, block));
   B.built = true;
+  return SPMVB_OK;
+}
+
+namespace {
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      p = nullptr;
+    }
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// 2-D view {m rows (contiguous), width slots} of a column-major ELL array,
+// boxes of 32 rows x width slots.
+bool encode_ell_map(CUtensorMap* tm, CUtensorMapDataType type, size_t elem, void* base, int m, int width) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(m), static_cast<cuuint64_t>(width)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(m) * elem};
+  const cuuint32_t box[2] = {32u, static_cast<cuuint32_t>(width)};
+  const cuuint32_t estr[2] = {1u, 1u};
+  return enc(tm, type, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+spmvb_status build_ell_tma(spmvb_matrix A, int max_width) {
+  std::lock_guard<std::mutex> lk(A->build_mu);
+  if (A->ell_tma_state != 0) return SPMVB_OK;
+  const char* e = std::getenv("SPMVB_ELL_STREAM");
+  const bool off = e && std::strcmp(e, "ldg") == 0;
+  const size_t es = dtype_size(A->dtype);
+  if (off || !A->ell_built || A->ell_width < 1 || A->ell_width > max_width || A->m % 4 != 0 || A->m < 32) {
+    A->ell_tma_state = -1;
+    return SPMVB_OK;
+  }
+  const bool ok =
+      encode_ell_map(&A->ell_tm_col, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, A->ell_colind.get(), A->m, A->ell_width) &&
+      encode_ell_map(&A->ell_tm_val, es == 8 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT64 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, es,
+                     A->ell_values.get(), A->m, A->ell_width);
+  A->ell_tma_state = ok ? 1 : -1;
   return SPMVB_OK;
 }
 

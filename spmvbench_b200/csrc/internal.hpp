@@ -2,6 +2,7 @@
 // context / matrix handles behind the C ABI (include/spmvb.h).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -126,6 +127,11 @@ struct spmvb_matrix_st {
   bool ell_built = false;
   int ell_width = 0;
   spmvb::DevBuf ell_colind, ell_values, ell_rowlen;
+  // TMA descriptors of the ELL arrays for ell_tma: state 0 = not built yet,
+  // 1 = ready, -1 = this matrix cannot use them (ell_rows runs).
+  int ell_tma_state = 0;
+  alignas(64) CUtensorMap ell_tm_col;
+  alignas(64) CUtensorMap ell_tm_val;
 
   // Hybrid ELL(K) + CSR tail
   bool hyb_built = false;
@@ -183,6 +189,10 @@ spmvb_status build_hyb(spmvb_matrix A, int forced_k);
 spmvb_status build_bcsr(spmvb_matrix A, int block);
 spmvb_status build_merge(spmvb_matrix A);
 spmvb_status build_buckets(spmvb_matrix A);
+// TMA descriptors for ell_tma (formats.cu); sets A->ell_tma_state. Needs the
+// ELL built; a matrix that does not qualify (width > max_width, m not a
+// multiple of 4, the stream variant switched off) gets state -1.
+spmvb_status build_ell_tma(spmvb_matrix A, int max_width);
 
 // On-device conversions (convert.cu): BCSR block x block (2 or 4) from the
 // uploaded CSR into A->bcsr2 / A->bcsr4, and the 4x4 block census of
@@ -218,6 +228,14 @@ spmvb_status check_err_word(spmvb_context ctx, cudaStream_t s);
 // memory, or pinned memory this device cannot address).
 inline bool stores_y_once(spmvb_kernel k) { return k != SPMVB_CSR_MERGE; }
 void* mapped_host_ptr(const void* h);
+
+// Power-iteration vector step (vecops.cu): *norm = the 2-norm of the m-entry
+// global vector held in x's padded layout (slot = owner * max_rows + local,
+// bounds on the device), in a fixed reduction order (partials:
+// norm_blocks(m) doubles); then every slot of x is multiplied by 1 / *norm.
+int norm_blocks(int64_t m);
+spmvb_status launch_norm_and_scale(spmvb_dtype dtype, void* x, int64_t m, const int* bounds, int nranks,
+                                   int max_rows, double* partials, double* norm, int sm_count, cudaStream_t s);
 
 // Peer-memory exchange launchers (peer.cu).
 spmvb_status peer_launch_ell(spmvb_matrix A, const PeerView& P, const void* x, cudaStream_t s);

@@ -29,6 +29,7 @@
 // and every other rank gives up too instead of reading stale x.
 #include <algorithm>
 #include <cstdint>
+#include <cstdlib>
 
 #include "internal.hpp"
 #include "spmv_kernels.cuh"
@@ -107,12 +108,40 @@ __device__ __forceinline__ void store_all(const PeerView& P, int i, T v) {
     if (q < P.nranks) static_cast<T*>(P.dst[q])[i] = v;
 }
 
+// Sum of ELL row `row` with up to 16 of its gathers in flight at once, left
+// to right from zero (the order of ell_row_sum, so the same bits).
+template <typename T>
+__device__ __forceinline__ T ell_row_sum16(const EllView& E, int row, int L, const T* __restrict__ x, uint64_t ps,
+                                           uint64_t pk) {
+  const T* __restrict__ vals = static_cast<const T*>(E.values);
+  T sum = T(0);
+  for (int j0 = 0; j0 < L; j0 += 16) {
+    T a[16], xv[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      if (j0 + u < L) {
+        const int64_t p = row + static_cast<int64_t>(j0 + u) * E.ld;
+        a[u] = ld_stream(vals + p, ps);
+        xv[u] = ld_keep(x + ld_stream(E.colind + p, ps), pk);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 16; ++u)
+      if (j0 + u < L) sum = add_rn(sum, mul_rn(a[u], xv[u]));
+  }
+  return sum;
+}
+
+// Rows are dealt round-robin over the grid; with a grid smaller than the
+// rows, each thread finishes its rows one after another, so the stores to
+// the peers leave while the rest of the step is still computing instead of
+// in one burst at the end.
 template <typename T>
 __global__ void __launch_bounds__(kPeerRowThreads) ell_rows_peer(EllView E, const T* __restrict__ x, PeerView P) {
   const uint64_t ps = policy_evict_first();
   const uint64_t pk = policy_evict_last();
   for (int row = blockIdx.x * blockDim.x + threadIdx.x; row < E.m; row += gridDim.x * blockDim.x)
-    store_all<T>(P, row, ell_row_sum<T, T>(E, row, E.row_lengths[row], x, ps, pk));
+    store_all<T>(P, row, ell_row_sum16<T>(E, row, E.row_lengths[row], x, ps, pk));
   peer_arrive(P);
 }
 
@@ -128,9 +157,20 @@ __global__ void peer_barrier(PeerView P) { peer_arrive(P); }
 }  // namespace
 
 // Grid of the grid-stride peer kernels: at most 8 CTAs of 256 threads per
-// SM, so few CTAs pay for the barrier's per-CTA release.
-static int peer_grid(int rows, int sm_count) {
-  return std::max(1, std::min((rows + 255) / 256, sm_count * 8));
+// SM, so few CTAs pay for the barrier's per-CTA release, and at least
+// `rows_per_thread` rows per thread (SPMVB_PEER_ROWS_PER_THREAD, default 1).
+static int peer_grid(int rows, int sm_count, int rows_per_thread = 1) {
+  const int per = std::max(1, rows_per_thread);
+  return std::max(1, std::min((rows + 256 * per - 1) / (256 * per), sm_count * 8));
+}
+
+static int peer_rows_per_thread() {
+  static const int v = [] {
+    const char* e = std::getenv("SPMVB_PEER_ROWS_PER_THREAD");
+    const int r = (e && *e) ? std::atoi(e) : 1;
+    return r > 0 ? r : 1;
+  }();
+  return v;
 }
 
 spmvb_status peer_launch_ell(spmvb_matrix A, const PeerView& P, const void* x, cudaStream_t s) {
@@ -143,7 +183,7 @@ spmvb_status peer_launch_ell(spmvb_matrix A, const PeerView& P, const void* x, c
   e.n = A->n;
   e.width = A->ell_width;
   e.ld = A->m;
-  const int grid = peer_grid(A->m, A->ctx->sm_count);
+  const int grid = peer_grid(A->m, A->ctx->sm_count, peer_rows_per_thread());
   if (A->dtype == SPMVB_F64)
     ell_rows_peer<double><<<grid, kPeerRowThreads, 0, s>>>(e, static_cast<const double*>(x), P);
   else

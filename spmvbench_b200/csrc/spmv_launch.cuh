@@ -5,6 +5,9 @@
 
 #include <algorithm>
 
+#include <cstdlib>
+
+#include "ell_tma.cuh"
 #include "internal.hpp"
 #include "spmm_kernels.cuh"
 #include "spmv_kernels.cuh"
@@ -24,6 +27,33 @@ static void launch_vector(const CsrView& v, int sms, const T* x, Acc* y,
   const int64_t need = (v.m + rows_per_block - 1) / rows_per_block;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(need, int64_t(sms) * 16)));
   csr_vector<T, Acc, G><<<grid, kRowThreads, 0, s>>>(v, x, y);
+}
+
+// ELL widths ell_tma serves (wider matrices run ell_rows).
+constexpr int kEllTmaMaxWidth = 16;
+
+// ell_tma with STAGES ring slots per warp on a persistent grid of as many
+// CTAs as fit on every SM (shared memory bounds it: 4 warps x STAGES slots
+// of 32 rows x width entries).
+template <typename T, typename Acc, int WMAX, int STAGES>
+static spmvb_status launch_ell_tma(spmvb_matrix A, const EllView& e, const T* x, Acc* y, cudaStream_t s) {
+  auto kern = ell_tma<T, Acc, WMAX, STAGES>;
+  constexpr int smem = kEllTmaWarps * STAGES * EllTmaStage<T, WMAX>::kBytes + 128;
+  static int per_sm = [&] {
+    int n = 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kEllTmaWarps * 32, smem) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+    return n;
+  }();
+  if (per_sm < 1) return fail(SPMVB_ERR_CUDA, "ell_tma cannot be resident on this device");
+  const int64_t warps_needed = (static_cast<int64_t>(A->m) + 31) / 32;
+  const int64_t ctas_needed = (warps_needed + kEllTmaWarps - 1) / kEllTmaWarps;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(ctas_needed, int64_t(A->ctx->sm_count) * per_sm)));
+  kern<<<grid, kEllTmaWarps * 32, smem, s>>>(A->ell_tm_col, A->ell_tm_val, e, x, y, A->ctx->err.as<int>());
+  return SPMVB_OK;
 }
 
 template <typename T, typename Acc>
@@ -83,7 +113,18 @@ spmvb_status launch_spmv(spmvb_matrix A, spmvb_kernel kernel, int lanes,
       e.n = A->n;
       e.width = A->ell_width;
       e.ld = A->m;
-      ell_rows<T, Acc, false><<<(A->m + kRowThreads - 1) / kRowThreads, kRowThreads, 0, stream>>>(e, x, y);
+      SPMVB_TRY(build_ell_tma(A, kEllTmaMaxWidth));
+      if (A->ell_tma_state == 1) {
+        // The matrix stream through the TMA engine, the gathers alone on the
+        // load path (ell_tma.cuh).
+        const char* st = std::getenv("SPMVB_ELL_TMA_STAGES");
+        const int stages = st ? std::atoi(st) : 3;
+        if (stages == 2) SPMVB_TRY((launch_ell_tma<T, Acc, kEllTmaMaxWidth, 2>(A, e, x, y, stream)));
+        else if (stages == 4) SPMVB_TRY((launch_ell_tma<T, Acc, kEllTmaMaxWidth, 4>(A, e, x, y, stream)));
+        else SPMVB_TRY((launch_ell_tma<T, Acc, kEllTmaMaxWidth, 3>(A, e, x, y, stream)));
+      } else {
+        ell_rows<T, Acc, false><<<(A->m + kRowThreads - 1) / kRowThreads, kRowThreads, 0, stream>>>(e, x, y);
+      }
       count_launch();
       break;
     }

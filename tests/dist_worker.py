@@ -81,6 +81,30 @@ for which, rows, kernel in ((2, 200000, S.ELL), (3, 300000, S.CSR_MERGE), (1, 0,
         print(f"rank {rank} workload {which} kernel {S.kernel_name(kernel)} exchange {exchange}: "
               f"{'ok' if ok else 'MISMATCH'}", flush=True)
         bad += not ok
+# Power iteration over the row blocks: the norm is taken over the whole
+# vector in a rank-independent order, so every rank's x and eigenvalue
+# estimate equal a one-rank run bit for bit (ELL keeps csr_omp's order).
+A = S.generate(2, seed=97, scale_rows=120000)
+x0 = S.generate_vector(98, A.n)
+D1 = S.DistMatrix(ctx, 1, 0, None, A, S.partition_rows(A.rowptr, 1), S.F64)
+D1.set_x(x0)
+lam1 = D1.power_iterate(8, kernel=S.ELL)
+x1 = D1.get_x()
+D1.close()
+bounds = S.partition_rows(A.rowptr, world)
+for exchange in ("nccl", "peer"):
+    obj = [S.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    D = S.DistMatrix(ctx, world, rank, obj[0], A, bounds, S.F64)
+    if exchange == "peer":
+        D.enable_peer()
+    D.set_x(x0)
+    lam = D.power_iterate(8, kernel=S.ELL)
+    ok = lam == lam1 and np.array_equal(D.get_x(), x1)
+    D.close()
+    print(f"rank {rank} power iteration exchange {exchange}: {'ok' if ok else 'MISMATCH'}", flush=True)
+    bad += not ok
+
 # Host-buffer product over the row blocks (spmvb_dist_pipeline): each rank
 # submits its rows' slice of x and must get its rows of csr_omp's y.
 for which, rows, kernel in ((2, 200000, S.ELL), (3, 300000, S.CSR_MERGE)):

@@ -107,6 +107,33 @@ def test_single_rank_iteration_matches_oracle(ctx):
     D.close()
 
 
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
+def test_power_iteration_single_rank(ctx, exchange):
+    """Power iteration x <- A x / ||A x|| on the sharded handle (one rank, both
+    exchanges): the eigenvalue estimate and x follow a CPU power iteration
+    built on the oracle's csr_omp within 1e-12, and a rerun is bit-identical."""
+    A = S.generate(2, seed=86, scale_rows=40000)
+    x0 = S.generate_vector(87, A.n)
+    D = S.DistMatrix(ctx, 1, 0, None, A, S.partition_rows(A.rowptr, 1), S.F64)
+    if exchange == "peer":
+        D.enable_peer()
+    runs = []
+    for _ in range(2):
+        D.set_x(x0)
+        lam = D.power_iterate(12, kernel=S.ELL)
+        runs.append((lam, D.get_x()))
+    assert runs[0][0] == runs[1][0]
+    assert_bitwise(runs[0][1], runs[1][1], "power iteration rerun")
+    x = x0.copy()
+    for _ in range(12):
+        y = oracle_y(A, x, S.F64, S.F64)
+        ref_lam = float(np.sqrt(np.dot(y, y)))
+        x = y / ref_lam
+    assert abs(runs[0][0] - ref_lam) <= 1e-12 * ref_lam
+    np.testing.assert_allclose(runs[0][1], x, rtol=1e-11, atol=1e-14)
+    D.close()
+
+
 @pytest.mark.parametrize("depth,kernel", [(1, "ELL"), (3, "ELL"), (3, "CSR_MERGE")])
 def test_dist_pipeline_single_rank_matches_oracle(ctx, depth, kernel):
     """The row-sharded host-buffer product with one rank: 6 calls with

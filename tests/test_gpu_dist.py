@@ -29,7 +29,7 @@ def test_two_rank_iteration_matches_oracle():
                           os.path.join(ROOT, "tests", "dist_worker.py")], env=env, capture_output=True, text=True,
                          timeout=400)
     assert out.returncode == 0, out.stdout[-3000:] + out.stderr[-3000:]
-    assert out.stdout.count(": ok") == 16, out.stdout[-3000:]
+    assert out.stdout.count(": ok") == 20, out.stdout[-3000:]
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
