@@ -220,10 +220,13 @@ class ClockSampler:
 # ------------------------------------------------------------------------------
 def csr_omp_runner(m, n, rowptr, colind, values, x, threads):
     """A callable running csr_omp once: the reference's own code when
-    oracle/_ref was built, else the C restatement; and its kind."""
+    oracle/_ref was built (its copy of the matrix first touched by the same
+    threads in csr_omp's row schedule, so on a host with several memory
+    nodes each thread reads local memory), else the C restatement; and its
+    kind."""
     import oracle
     if oracle.ref_available():
-        R = oracle.RefCsr(m, n, rowptr, colind, values)
+        R = oracle.RefCsr(m, n, rowptr, colind, values, place_threads=threads)
         y = np.empty(m)
         return (lambda: R.spmv(x, np.float64, threads, out=y)), "reference"  # noqa: E731
     return (lambda: oracle.spmv_csr(m, rowptr, colind, values, x, np.float64, threads)), "port"  # noqa: E731

@@ -305,8 +305,11 @@ bool encode_ell_map(CUtensorMap* tm, CUtensorMapDataType type, size_t elem, void
 spmvb_status build_ell_tma(spmvb_matrix A, int max_width) {
   std::lock_guard<std::mutex> lk(A->build_mu);
   if (A->ell_tma_state != 0) return SPMVB_OK;
+  // ell_rows (plain loads) is the default: on B200 it measured faster than
+  // ell_tma on the uniform 1M-row matrix (68.7 us against 71.0 us with a
+  // 4-slot ring, 112 us with 2 or 3). SPMVB_ELL_STREAM=tma selects ell_tma.
   const char* e = std::getenv("SPMVB_ELL_STREAM");
-  const bool off = e && std::strcmp(e, "ldg") == 0;
+  const bool off = !(e && std::strcmp(e, "tma") == 0);
   const size_t es = dtype_size(A->dtype);
   if (off || !A->ell_built || A->ell_width < 1 || A->ell_width > max_width || A->m % 4 != 0 || A->m < 32) {
     A->ell_tma_state = -1;

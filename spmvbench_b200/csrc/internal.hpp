@@ -191,7 +191,7 @@ spmvb_status build_merge(spmvb_matrix A);
 spmvb_status build_buckets(spmvb_matrix A);
 // TMA descriptors for ell_tma (formats.cu); sets A->ell_tma_state. Needs the
 // ELL built; a matrix that does not qualify (width > max_width, m not a
-// multiple of 4, the stream variant switched off) gets state -1.
+// multiple of 4) or a process without SPMVB_ELL_STREAM=tma gets state -1.
 spmvb_status build_ell_tma(spmvb_matrix A, int max_width);
 
 // On-device conversions (convert.cu): BCSR block x block (2 or 4) from the

@@ -118,7 +118,7 @@ spmvb_status launch_spmv(spmvb_matrix A, spmvb_kernel kernel, int lanes,
         // The matrix stream through the TMA engine, the gathers alone on the
         // load path (ell_tma.cuh).
         const char* st = std::getenv("SPMVB_ELL_TMA_STAGES");
-        const int stages = st ? std::atoi(st) : 3;
+        const int stages = st ? std::atoi(st) : 4;
         if (stages == 2) SPMVB_TRY((launch_ell_tma<T, Acc, kEllTmaMaxWidth, 2>(A, e, x, y, stream)));
         else if (stages == 4) SPMVB_TRY((launch_ell_tma<T, Acc, kEllTmaMaxWidth, 4>(A, e, x, y, stream)));
         else SPMVB_TRY((launch_ell_tma<T, Acc, kEllTmaMaxWidth, 3>(A, e, x, y, stream)));

@@ -147,3 +147,47 @@ def test_spmm_timings(tmp_path):
     assert out.returncode == 0, out.stdout + out.stderr
     assert out.stdout.count("GFLOP/s") == 7 and "wrote results/spmm.csv" in out.stdout
     assert "cusparse_spmm" in out.stdout and out.stdout.count("x cuSPARSE") == 6
+
+
+def test_validate_criterion_against_scipy_catches_a_perturbed_y():
+    """--validate's checks on the CPU: SciPy's product is the reference
+    (independent of this library and of the oracle), an unchanged copy
+    passes, and one row moved by more than the gamma_n bound - or a NaN, or a
+    last-bit change where bit equality is required - is reported."""
+    import numpy as np
+
+    import spmvbench_b200 as S
+    from spmvbench_b200 import driver as D
+    A = S.generate(3, seed=5, scale_rows=20000)
+    x = S.generate_vector(6, A.n)
+    ref = D.scipy_product(A, A.values, x)
+    assert D.row_bound_failures(A.rowptr, A.colind, A.values, x, ref, ref.copy(), 2.0 ** -53, 1e-12).size == 0
+    bad = ref.copy()
+    i = int(np.argmax(np.diff(A.rowptr)))
+    bad[i] += 1e-9 * (abs(ref[i]) + 1.0)
+    assert D.row_bound_failures(A.rowptr, A.colind, A.values, x, ref, bad, 2.0 ** -53, 1e-12).tolist() == [i]
+    nan = ref.copy()
+    nan[7] = np.nan
+    assert 7 in D.row_bound_failures(A.rowptr, A.colind, A.values, x, ref, nan, 2.0 ** -53, 1e-12).tolist()
+    ulp = ref.copy()
+    ulp[3] = np.nextafter(ulp[3], np.inf)
+    assert not np.array_equal(ulp, ref)  # what the bit-exact kernels are held to
+    st = D.err_stats(bad, ref)
+    assert st["max_abs_err"] > 0 and st["max_rel_err"] > 0 and st["l2_rel_err"] > 0
+    assert D.err_stats(ref, ref) == {"max_rel_err": 0.0, "l2_rel_err": 0.0, "max_abs_err": 0.0}
+
+
+def test_scipy_product_is_csr_omp_bitwise():
+    """SciPy's float64 CSR product adds each row left to right like csr_omp,
+    so the bit-exact GPU kernels are held to equality with it (the reference's
+    own validate gate found max_rel 0 against SciPy)."""
+    import numpy as np
+
+    import oracle
+    import spmvbench_b200 as S
+    from spmvbench_b200 import driver as D
+    for which, rows in ((1, 0), (2, 30000), (4, 8000)):
+        A = S.generate(which, seed=9, scale_rows=rows)
+        x = S.generate_vector(10, A.n)
+        assert np.array_equal(D.scipy_product(A, A.values, x),
+                              oracle.spmv_csr(A.m, A.rowptr, A.colind, A.values, x, np.float64))

@@ -342,3 +342,23 @@ def test_device_row_stats_equal_host_on_workloads(ctx, which):
     host, dev = S.row_stats(A), M.row_stats()
     assert host == dev
     M.close()
+
+
+@pytest.mark.parametrize("which,rows", [(2, 200000), (1, 0), (2, 100004), (2, 100002), (4, 40000)])
+@pytest.mark.parametrize("stages", ["2", "3", "4"])
+def test_ell_tma_stream_is_bit_identical(ctx, monkeypatch, which, rows, stages):
+    """The ELL kernel whose matrix stream goes through the TMA engine
+    (SPMVB_ELL_STREAM=tma, per-warp ring of STAGES slots): bit-identical to
+    csr_omp in every (storage, accumulator) pair, on widths 9 and 16, a row
+    count that is not a multiple of 32 (100,004: the last chunk's copy
+    reaches past m), and where ell_rows runs instead (m = 100,002 not a
+    multiple of 4; width 32)."""
+    monkeypatch.setenv("SPMVB_ELL_STREAM", "tma")
+    monkeypatch.setenv("SPMVB_ELL_TMA_STAGES", stages)
+    A = S.generate(which, seed=57, scale_rows=rows)
+    x = mixed_x(A.n, seed=58)
+    for dt, acc in DTYPE_PAIRS:
+        M = S.DeviceMatrix(ctx, A, dt)
+        assert_bitwise(oracle_y(A, x, dt, acc), run_spmv(M, x, S.ELL, acc=acc), f"ell tma {dt}/{acc}")
+        M.close()
+    ctx.check()  # no bounded wait gave up
