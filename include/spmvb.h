@@ -254,6 +254,15 @@ spmvb_status spmvb_spmv_merge_noalloc(spmvb_dtype dtype, int32_t m, int32_t n,
 spmvb_status spmvb_spmm(spmvb_matrix A, int tile, int bucketed, int k,
                         const void* d_X, void* d_Y, spmvb_dtype acc,
                         void* stream);
+/* Column bands of the plain SpMM (tile 64, X 16-byte aligned, k a multiple
+ * of 16 bytes / element size, every row's columns ascending): with bands > 1
+ * the product is swept in `bands` passes, pass b adding each row's entries
+ * whose column lies in the b-th band of n / bands columns, so the X rows a
+ * pass gathers fit the L2. Each output element still receives its terms in
+ * CSR order (bit-identical to the one-pass kernel); Y is read and written
+ * once per pass. 0 = automatic (the default), 1 = one pass. No reference
+ * counterpart (its tiled kernel re-reads X per row, src/cuda/spmm_cuda.cu:31-60). */
+spmvb_status spmvb_matrix_set_spmm_bands(spmvb_matrix A, int bands);
 /* Host-buffer form (H2D X, kernel, D2H Y). Replaces run_tiled's data path
  * (src/cuda/spmm_cuda.cu:214-325) without its per-call malloc/free. */
 spmvb_status spmvb_spmm_host(spmvb_matrix A, int tile, int bucketed, int k,

@@ -358,6 +358,11 @@ class DeviceMatrix:
         call("spmvb_spmv", self.handle, kernel, lanes, block, C.c_void_p(x.data_ptr()),
              C.c_void_p(y.data_ptr()), acc, _stream_ptr(stream))
 
+    def set_spmm_bands(self, bands: int) -> None:
+        """Column bands of the plain tile-64 SpMM sweep (0 = automatic,
+        1 = one row-order pass); bit-identical results either way."""
+        call("spmvb_matrix_set_spmm_bands", self.handle, bands)
+
     def spmm(self, X, Y, k: int, tile: int = 32, bucketed: bool = False,
              acc: int | None = None, stream=None) -> None:
         acc = self.dtype if acc is None else acc

@@ -95,6 +95,7 @@ SIGNATURES = {
     "spmvb_spmv_merge_noalloc": (C.c_int, [C.c_int, C.c_int32, C.c_int32, C.c_int64, P, P, P, P, P,
                                            C.c_int, P]),
     "spmvb_spmm": (C.c_int, [P, C.c_int, C.c_int, C.c_int, P, P, C.c_int, P]),
+    "spmvb_matrix_set_spmm_bands": (C.c_int, [P, C.c_int]),
     "spmvb_spmm_host": (C.c_int, [P, C.c_int, C.c_int, C.c_int, P, P, C.c_int, P]),
     "spmvb_probe_gather_rate": (C.c_int, [P, C.c_int64, C.c_int64, C.POINTER(C.c_double)]),
     "spmvb_compute_row_stats": (C.c_int, [P, P, C.c_int32, C.c_int32, C.c_int64,

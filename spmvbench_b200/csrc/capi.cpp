@@ -248,6 +248,13 @@ spmvb_status spmvb_matrix_create_csr(spmvb_context ctx, spmvb_dtype dtype, int32
   A->max_row = max_row;
   const size_t es = dtype_size(dtype);
   A->h_rowptr.assign(h_rowptr, h_rowptr + m + 1);
+  A->sorted_rows = true;
+  for (int32_t i = 0; i < m && A->sorted_rows; ++i)
+    for (int32_t p = h_rowptr[i] + 1; p < h_rowptr[i + 1]; ++p)
+      if (h_colind[p] < h_colind[p - 1]) {
+        A->sorted_rows = false;
+        break;
+      }
   if (nnz > 0) {
     A->h_colind.assign(h_colind, h_colind + nnz);
     const auto* vb = static_cast<const unsigned char*>(h_values);
@@ -261,6 +268,14 @@ spmvb_status spmvb_matrix_create_csr(spmvb_context ctx, spmvb_dtype dtype, int32
     return s;
   }
   *out = A;
+  return SPMVB_OK;
+}
+
+spmvb_status spmvb_matrix_set_spmm_bands(spmvb_matrix A, int bands) {
+  clear_error();
+  if (!A) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null matrix");
+  if (bands < 0 || bands > 64) return fail(SPMVB_ERR_INVALID_ARGUMENT, "bands must be in [0, 64]");
+  A->spmm_bands = bands;
   return SPMVB_OK;
 }
 

@@ -48,6 +48,21 @@ __global__ void merge_partition(CsrView A, int64_t num_items, int tile_items,
   tile_row[t] = static_cast<int>(lo);
 }
 
+__global__ void spmm_band_splits(CsrView A, int bands, int band_cols, int* __restrict__ split) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= A.m) return;
+  const int s = A.rowptr[i], e = A.rowptr[i + 1];
+  for (int b = 1; b < bands; ++b) {
+    const int64_t bound = static_cast<int64_t>(b) * band_cols;
+    int lo = s, hi = e;  // first p in [s, e) with colind[p] >= bound
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (A.colind[mid] < bound) lo = mid + 1; else hi = mid;
+    }
+    split[static_cast<int64_t>(b - 1) * A.m + i] = lo;
+  }
+}
+
 // Copies each row's first min(len, cap) entries into column-major slots and
 // records row lengths (len, or -1 when len > cap and long_marker is set).
 template <typename W>
@@ -320,6 +335,24 @@ spmvb_status build_ell_tma(spmvb_matrix A, int max_width) {
       encode_ell_map(&A->ell_tm_val, es == 8 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT64 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, es,
                      A->ell_values.get(), A->m, A->ell_width);
   A->ell_tma_state = ok ? 1 : -1;
+  return SPMVB_OK;
+}
+
+spmvb_status build_band_splits(spmvb_matrix A, int bands) {
+  std::lock_guard<std::mutex> lk(A->build_mu);
+  if (A->band_count == bands) return SPMVB_OK;
+  DeviceGuard g(A->device);
+  A->band_count = 0;
+  A->band_split.reset();
+  if (bands > 1) {
+    SPMVB_TRY(A->band_split.alloc(static_cast<size_t>(bands - 1) * std::max(A->m, 1) * 4));
+    const int band_cols = (A->n + bands - 1) / bands;
+    spmm_band_splits<<<(A->m + 255) / 256, 256>>>(A->csr_view(), bands, band_cols, A->band_split.as<int>());
+    count_launch();
+    SPMVB_TRY_CUDA(cudaGetLastError());
+    SPMVB_TRY_CUDA(cudaStreamSynchronize(0));
+  }
+  A->band_count = bands;
   return SPMVB_OK;
 }
 

@@ -158,6 +158,14 @@ struct spmvb_matrix_st {
   int merge_tiles = 0;
   spmvb::DevBuf merge_tile_row, merge_carry_row, merge_carry_val;
 
+  // SpMM column bands: rows' entries split at band_count - 1 column
+  // boundaries ((band_count - 1) x m ints); band_count 0 = not built.
+  // sorted_rows: every row's columns ascend (the band sweep needs it).
+  int band_count = 0;
+  bool sorted_rows = false;
+  int spmm_bands = 0;  // requested band count (0 = automatic)
+  spmvb::DevBuf band_split;
+
   // SpMM row buckets
   bool buckets_built = false;
   int b_short = 0, b_med = 0, b_long = 0;
@@ -189,6 +197,8 @@ spmvb_status build_hyb(spmvb_matrix A, int forced_k);
 spmvb_status build_bcsr(spmvb_matrix A, int block);
 spmvb_status build_merge(spmvb_matrix A);
 spmvb_status build_buckets(spmvb_matrix A);
+// Row split points of the SpMM column-band sweep for `bands` bands.
+spmvb_status build_band_splits(spmvb_matrix A, int bands);
 // TMA descriptors for ell_tma (formats.cu); sets A->ell_tma_state. Needs the
 // ELL built; a matrix that does not qualify (width > max_width, m not a
 // multiple of 4) or a process without SPMVB_ELL_STREAM=tma gets state -1.

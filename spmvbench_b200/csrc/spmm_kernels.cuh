@@ -139,6 +139,93 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Column-band pass of the plain SpMM (spmm_bands in spmv_launch.cuh): the
+// columns of A (rows of X) are cut into bands that fit the L2 and the whole
+// product is swept band by band, so the X rows one pass gathers stay
+// resident. Row i's entries of band b are [start, end) = split[b-1][i] ..
+// split[b][i] (rowptr ends at b = 0 and b = B-1). Pass 0 starts each output
+// from zero; later passes load the running values of Y and keep adding. The
+// rows' columns are ascending, so every output element still receives its
+// terms left to right in CSR order, as spmm_csr_cpu adds them: bit-identical.
+// X is gathered with L2 evict-last, Y and A streamed with evict-first.
+template <typename T, typename Acc, int G, int W, bool VEC>
+__global__ void __launch_bounds__(256)
+    spmm_band(CsrView A, const int* __restrict__ lo_split, const int* __restrict__ hi_split, bool first,
+              const T* __restrict__ X, Acc* __restrict__ Y, int k) {
+  constexpr int TILE = G * W;
+  constexpr int RPW = kWarp / G;
+  const T* __restrict__ vals = static_cast<const T*>(A.values);
+  const uint64_t ps = policy_evict_first();
+  const uint64_t pk = policy_evict_last();
+  const int lane = threadIdx.x & (kWarp - 1);
+  const int gl = lane & (G - 1);
+  const int grp = lane / G;
+  const unsigned mask = (G == kWarp) ? 0xffffffffu : (((1u << G) - 1u) << (grp * G));
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / kWarp;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * blockDim.x / kWarp;
+  for (int64_t r0 = warp * RPW; r0 < A.m; r0 += nwarps * RPW) {
+    const int64_t row = r0 + grp;
+    const bool valid = row < A.m;
+    const int s = valid ? (lo_split ? lo_split[row] : A.rowptr[row]) : 0;
+    const int e = valid ? (hi_split ? hi_split[row] : A.rowptr[row + 1]) : 0;
+    Acc* yrow = Y + row * k;
+    for (int t0 = 0; t0 < k; t0 += TILE) {
+      Acc acc[W];
+#pragma unroll
+      for (int w = 0; w < W; ++w) {
+        const int col = lane_col<G, W, VEC>(t0, gl, w);
+        acc[w] = (!first && valid && col < k) ? ld_stream(yrow + col, ps) : Acc(0);
+      }
+      for (int p0 = s; p0 < e; p0 += G) {
+        int my_c = 0;
+        T my_a = T(0);
+        if (p0 + gl < e) {
+          my_c = ld_stream(A.colind + p0 + gl, ps);
+          my_a = ld_stream(vals + p0 + gl, ps);
+        }
+        const int cnt = min(G, e - p0);
+        int j = 0;
+        for (; j + 4 <= cnt; j += 4) {
+          int c[4];
+          T a[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            c[u] = __shfl_sync(mask, my_c, j + u, G);
+            a[u] = __shfl_sync(mask, my_a, j + u, G);
+          }
+          T xv[4][W];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) gather_xrow<T, W, G, VEC>(X, c[u], k, t0, gl, pk, xv[u]);
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int w = 0; w < W; ++w) acc[w] = add_rn(acc[w], prod<Acc>(a[u], xv[u][w]));
+        }
+        for (; j < cnt; ++j) {
+          const int c = __shfl_sync(mask, my_c, j, G);
+          const T a = __shfl_sync(mask, my_a, j, G);
+          T xv[W];
+          gather_xrow<T, W, G, VEC>(X, c, k, t0, gl, pk, xv);
+#pragma unroll
+          for (int w = 0; w < W; ++w) acc[w] = add_rn(acc[w], prod<Acc>(a, xv[w]));
+        }
+      }
+      if (valid) {
+#pragma unroll
+        for (int w = 0; w < W; ++w) {
+          const int col = lane_col<G, W, VEC>(t0, gl, w);
+          if (col < k) st_stream(yrow + col, acc[w]);
+        }
+      }
+    }
+  }
+}
+
+// Band boundaries of every row: split[(b - 1) * m + i] = the first entry of
+// row i with column >= b * band_cols (b = 1 .. bands-1), by binary search
+// over the row's ascending columns.
+__global__ void spmm_band_splits(CsrView A, int bands, int band_cols, int* __restrict__ split);
+
 // Long rows (bucketed variant): one CTA of 8 warps per row; warp w takes the
 // w-th contiguous eighth of the row's entries, partial tiles meet in shared
 // memory and are added in warp order.

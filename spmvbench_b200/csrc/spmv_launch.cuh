@@ -229,6 +229,34 @@ static void launch_spmm_tile(const CsrView& v, int tile, const int* rows,
   }
 }
 
+// Column bands of the plain SpMM sweep: the handle's setting
+// (spmvb_matrix_set_spmm_bands; 1 = one row-order pass), or with 0 (auto)
+// a single pass.
+static int spmm_band_count(spmvb_matrix A, int k, size_t es) {
+  if (A->spmm_bands > 0) return A->spmm_bands;
+  (void)k;
+  (void)es;
+  return 1;
+}
+
+// The plain SpMM swept in `bands` column bands (spmm_band): one launch per
+// band, stream-ordered, each carrying Y over from the previous one.
+template <typename T, typename Acc, int G, int W, bool VEC>
+static void launch_spmm_bands(spmvb_matrix A, int bands, int sms, const T* X, Acc* Y, int k, cudaStream_t s) {
+  const CsrView v = A->csr_view();
+  const int64_t rows_per_block = (kRowThreads / kWarp) * (kWarp / G);
+  const int64_t need = (A->m + rows_per_block - 1) / rows_per_block;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(need, int64_t(sms) * 16)));
+  const int* split = A->band_split.as<int>();
+  const int64_t m = A->m;
+  for (int b = 0; b < bands; ++b) {
+    const int* lo = b == 0 ? nullptr : split + (b - 1) * m;
+    const int* hi = b == bands - 1 ? nullptr : split + b * m;
+    spmm_band<T, Acc, G, W, VEC><<<grid, kRowThreads, 0, s>>>(v, lo, hi, b == 0, X, Y, k);
+  }
+  count_launch(bands);
+}
+
 template <typename T, typename Acc>
 spmvb_status launch_spmm(spmvb_matrix A, int tile, int bucketed, int k,
                          const T* X, Acc* Y, cudaStream_t stream) {
@@ -239,7 +267,11 @@ spmvb_status launch_spmm(spmvb_matrix A, int tile, int bucketed, int k,
   // Reference tile selection: 16, 64, anything else -> 32 (src/cuda/spmm_cuda.cu:155-168).
   const int t = (tile == 16 || tile == 64) ? tile : 32;
   const bool vec = (k % V) == 0 && (reinterpret_cast<uintptr_t>(X) % 16) == 0;
-  if (!bucketed) {
+  const int bands = (!bucketed && A->sorted_rows && vec && t == 64) ? spmm_band_count(A, k, sizeof(T)) : 1;
+  if (bands > 1) {
+    SPMVB_TRY(build_band_splits(A, bands));
+    launch_spmm_bands<T, Acc, 64 / V, V, true>(A, bands, sms, X, Y, k, stream);
+  } else if (!bucketed) {
     if (vec) launch_spmm_tile<T, Acc, true>(v, t, nullptr, A->m, sms, X, Y, k, stream);
     else launch_spmm_tile<T, Acc, false>(v, t, nullptr, A->m, sms, X, Y, k, stream);
   } else {
