@@ -441,15 +441,13 @@ __global__ void __launch_bounds__(256)
 //
 // ELL blocks: one thread per row with len <= K, csr_omp order (bit-identical).
 //
-// Chunk blocks: a fixed set of CTAs whose warps walk the chunks (at most
-// kHybChunk entries each) round-robin; a warp loads the bounds, row ids and
-// entries of its next chunk before it gathers and sums the current one, so
-// those loads are in flight during the current chunk's dependency chain.
-// Within a chunk lane l loads entries l, l+32, ... (coalesced) and every
-// gather of the chunk is in flight before any product is formed.
+// Chunk blocks, one warp per chunk of at most kHybChunk entries: lane l loads
+// entries l, l+32, ... (coalesced) and every gather of the chunk is in flight
+// before any product is formed.
 //  - Packed chunk (whole rows): the products go to the warp's slice of shared
 //    memory and lane l adds rows chunk_row[c]+l, +l+32, ... left to right from
-//    zero, the csr_omp order, so these rows are bit-identical too.
+//    zero, the csr_omp order, so these rows are bit-identical too. The lane's
+//    first row's bounds and id are loaded with the chunk's entries.
 //  - Segment of a row longer than kHybChunk: the warp reduces it in a fixed
 //    order (lane partials over p = l + 32i, then a butterfly) into partial[c];
 //    the warp whose partial completes the row (per-row counter) adds the
@@ -457,44 +455,6 @@ __global__ void __launch_bounds__(256)
 //    Deterministic, re-associated (bounded by 2*gamma_n*sum|a_ij x_j|).
 //
 // Remaining blocks: y = 0 for the empty rows when K = 0.
-template <typename T, int PER>
-struct HybChunk {
-  int64_t e0 = 0;
-  int span = 0;
-  int li0 = 0, li_end = 0;
-  int64_t rs0 = 0, re0 = 0;   // first row's bounds (a cut row's, for a segment)
-  int64_t my_s = 0, my_e = 0;  // this lane's first row of a packed chunk
-  int my_row = 0;
-  int col[PER];
-  T val[PER];
-};
-
-template <typename T, int PER>
-__device__ __forceinline__ void hyb_load_chunk(const HybView& H, int c, int lane, uint64_t ps,
-                                               HybChunk<T, PER>& k) {
-  const T* __restrict__ tv = static_cast<const T*>(H.tail_values);
-  k.e0 = H.chunk_start[c];
-  k.span = static_cast<int>(H.chunk_start[c + 1] - k.e0);
-  k.li0 = H.chunk_row[c];
-  k.li_end = H.chunk_row[c + 1];  // packed: rows li0 .. li_end-1
-#pragma unroll
-  for (int i = 0; i < PER; ++i) {
-    const int q = lane + i * kWarp;
-    k.col[i] = q < k.span ? ld_stream(H.tail_colind + k.e0 + q, ps) : 0;
-    k.val[i] = q < k.span ? ld_stream(tv + k.e0 + q, ps) : T(0);
-  }
-  k.rs0 = H.tail_ptr[k.li0];
-  k.re0 = H.tail_ptr[k.li0 + 1];
-  const int my = k.li0 + lane;
-  k.my_s = k.my_e = 0;
-  k.my_row = 0;
-  if (my < k.li_end) {
-    k.my_s = H.tail_ptr[my];
-    k.my_e = H.tail_ptr[my + 1];
-    k.my_row = H.long_rows[my];
-  }
-}
-
 template <typename T, typename Acc>
 __global__ void __launch_bounds__(256)
     hyb_rows(HybView H, const T* __restrict__ x, Acc* __restrict__ y) {
@@ -519,69 +479,81 @@ __global__ void __launch_bounds__(256)
   }
   const int wib = threadIdx.x / kWarp;
   const int lane = threadIdx.x & (kWarp - 1);
-  const int stride = H.chunk_blocks * W;
-  int c = cb_index * W + wib;
+  const int c = cb_index * W + wib;
   if (c >= H.n_chunks) return;
-  HybChunk<T, PER> cur, nxt;
-  hyb_load_chunk<T, PER>(H, c, lane, ps, cur);
-  for (;;) {
-    const int cn = c + stride;
-    if (cn < H.n_chunks) hyb_load_chunk<T, PER>(H, cn, lane, ps, nxt);
-    Acc pr[PER];
-#pragma unroll
-    for (int i = 0; i < PER; ++i)
-      pr[i] = (lane + i * kWarp < cur.span) ? prod<Acc>(cur.val[i], ld_keep(x + cur.col[i], pk)) : Acc(0);
+  const T* __restrict__ tv = static_cast<const T*>(H.tail_values);
+  const int64_t e0 = H.chunk_start[c];
+  const int span = static_cast<int>(H.chunk_start[c + 1] - e0);
+  const int li0 = H.chunk_row[c];
+  const int li_end = H.chunk_row[c + 1];  // packed: rows li0 .. li_end-1
 
-    if (cur.re0 - cur.rs0 > kHybChunk) {
-      // Segment of a cut row.
-      Acc v = Acc(0);
+  int col[PER];
+  T val[PER];
 #pragma unroll
-      for (int i = 0; i < PER; ++i) v = add_rn(v, pr[i]);  // entries past the span add exact zeros
-      v = group_sum<kWarp>(v);
-      Acc* part = static_cast<Acc*>(H.partial);
-      const int si = H.chunk_split[c];
-      const int first = H.split_first[si];
-      const int pieces = static_cast<int>((cur.re0 - cur.rs0 + kHybChunk - 1) / kHybChunk);
-      int last = 0;
-      if (lane == 0) {
-        part[c] = v;
-        __threadfence();  // the partial is visible before the count
-        last = atomicAdd(H.split_count + si, 1) == pieces - 1;
-      }
-      if (__shfl_sync(0xffffffffu, last, 0)) {
-        __threadfence();
-        Acc t = Acc(0);
-        for (int k = lane; k < pieces; k += kWarp) t = add_rn(t, __ldcg(part + first + k));
-        t = group_sum<kWarp>(t);
-        if (lane == 0) {
-          y[H.long_rows[cur.li0]] = t;
-          H.split_count[si] = 0;  // ready for the next launch
-        }
-      }
-    } else {
-      // Packed chunk: whole rows.
+  for (int i = 0; i < PER; ++i) {
+    const int q = lane + i * kWarp;
+    col[i] = q < span ? ld_stream(H.tail_colind + e0 + q, ps) : 0;
+    val[i] = q < span ? ld_stream(tv + e0 + q, ps) : T(0);
+  }
+  const int64_t rs0 = H.tail_ptr[li0];
+  const int64_t re0 = H.tail_ptr[li0 + 1];
+  // The lane's first row (packed chunks), loaded alongside the entries.
+  const int my = li0 + lane;
+  int64_t my_s = 0, my_e = 0;
+  int my_row = 0;
+  if (my < li_end) {
+    my_s = H.tail_ptr[my];
+    my_e = H.tail_ptr[my + 1];
+    my_row = H.long_rows[my];
+  }
+  Acc pr[PER];
 #pragma unroll
-      for (int i = 0; i < PER; ++i) s_prod[wib][swz<Acc>(lane + i * kWarp)] = pr[i];
-      __syncwarp();
-      int64_t my_s = cur.my_s, my_e = cur.my_e;
-      int my_row = cur.my_row;
-      for (int li = cur.li0 + lane; li < cur.li_end; li += kWarp) {
-        if (li != cur.li0 + lane) {
-          my_s = H.tail_ptr[li];
-          my_e = H.tail_ptr[li + 1];
-          my_row = H.long_rows[li];
-        }
-        const int a = static_cast<int>(my_s - cur.e0);
-        const int b = static_cast<int>(my_e - cur.e0);
-        Acc v = Acc(0);
-        for (int q = a; q < b; ++q) v = add_rn(v, s_prod[wib][swz<Acc>(q)]);
-        y[my_row] = v;
-      }
-      __syncwarp();  // row sums read before the next chunk's products land
+  for (int i = 0; i < PER; ++i)
+    pr[i] = (lane + i * kWarp < span) ? prod<Acc>(val[i], ld_keep(x + col[i], pk)) : Acc(0);
+
+  if (re0 - rs0 > kHybChunk) {
+    // Segment of a cut row.
+    Acc v = Acc(0);
+#pragma unroll
+    for (int i = 0; i < PER; ++i) v = add_rn(v, pr[i]);  // entries past the span add exact zeros
+    v = group_sum<kWarp>(v);
+    Acc* part = static_cast<Acc*>(H.partial);
+    const int si = H.chunk_split[c];
+    const int first = H.split_first[si];
+    const int pieces = static_cast<int>((re0 - rs0 + kHybChunk - 1) / kHybChunk);
+    int last = 0;
+    if (lane == 0) {
+      part[c] = v;
+      __threadfence();  // the partial is visible before the count
+      last = atomicAdd(H.split_count + si, 1) == pieces - 1;
     }
-    if (cn >= H.n_chunks) break;
-    cur = nxt;
-    c = cn;
+    if (__shfl_sync(0xffffffffu, last, 0)) {
+      __threadfence();
+      Acc t = Acc(0);
+      for (int k = lane; k < pieces; k += kWarp) t = add_rn(t, __ldcg(part + first + k));
+      t = group_sum<kWarp>(t);
+      if (lane == 0) {
+        y[H.long_rows[li0]] = t;
+        H.split_count[si] = 0;  // ready for the next launch
+      }
+    }
+    return;
+  }
+  // Packed chunk: whole rows.
+#pragma unroll
+  for (int i = 0; i < PER; ++i) s_prod[wib][swz<Acc>(lane + i * kWarp)] = pr[i];
+  __syncwarp();
+  for (int li = my; li < li_end; li += kWarp) {
+    if (li != my) {
+      my_s = H.tail_ptr[li];
+      my_e = H.tail_ptr[li + 1];
+      my_row = H.long_rows[li];
+    }
+    const int a = static_cast<int>(my_s - e0);
+    const int b = static_cast<int>(my_e - e0);
+    Acc v = Acc(0);
+    for (int q = a; q < b; ++q) v = add_rn(v, s_prod[wib][swz<Acc>(q)]);
+    y[my_row] = v;
   }
 }
 

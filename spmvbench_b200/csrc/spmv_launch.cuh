@@ -156,20 +156,7 @@ spmvb_status launch_spmv(spmvb_matrix A, spmvb_kernel kernel, int lanes,
       h.n_split = A->hyb_n_split;
       h.n_empty = A->hyb_n_empty;
       h.ell_blocks = A->hyb_K > 0 ? (A->m + kRowThreads - 1) / kRowThreads : 0;
-      {
-        // Chunk CTAs: as many as are resident at once (each warp walks
-        // chunks round-robin), never more than there are chunks to share.
-        static int per_sm = [] {
-          int n = 0;
-          if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, hyb_rows<T, Acc>, kRowThreads, 0) != cudaSuccess) {
-            cudaGetLastError();
-            n = 4;
-          }
-          return std::max(1, n);
-        }();
-        const int needed = (h.n_chunks + kRowThreads / kWarp - 1) / (kRowThreads / kWarp);
-        h.chunk_blocks = std::min(needed, sms * per_sm);
-      }
+      h.chunk_blocks = (h.n_chunks + kRowThreads / kWarp - 1) / (kRowThreads / kWarp);
       const int empty_blocks = (h.n_empty + kRowThreads - 1) / kRowThreads;
       const int grid = h.ell_blocks + h.chunk_blocks + empty_blocks;
       if (grid > 0) {
