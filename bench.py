@@ -24,7 +24,8 @@ Extra objects on the same line:
                 measured live by spmvb_probe_gather_rate)
   cpu_baseline  the reference's own csr_omp (oracle/_ref, compiled from the
                 reference sources; the C restatement if that is absent) on
-                the same matrix, all host threads, rank 0 at N=1
+                the same matrix, all host threads, rank 0 at N=1: the
+                reference arm's command run in a separate process (400 steps)
   e2e           the same product through the host-buffer API: every rank
                 copies its rows' slice of x in from pinned host memory, the
                 slices are all-gathered over NVLink, and each rank's rows of y
@@ -112,13 +113,30 @@ def host_threads() -> int:
 
 
 def prepare_cpu_run():
-    """Before the oracle's OpenMP runtime first loads: all host CPUs back in
-    this thread's mask (torch's own runtime may have narrowed it) and the
-    threads bound to neighbouring cores (OMP_PROC_BIND=close, read when the
-    runtime starts)."""
+    """Before the oracle's OpenMP runtime first loads (a process without
+    torch, whose own runtime would be picked up instead): all host CPUs in
+    this thread's mask and the threads bound to neighbouring cores
+    (OMP_PROC_BIND=close, read when the runtime starts)."""
     if HOST_CPUS:
         os.sched_setaffinity(0, HOST_CPUS)
     os.environ["OMP_PROC_BIND"] = "close"
+
+
+def cpu_baseline_in_clean_process(steps: int) -> dict:
+    """The reference arm's own command (`--impl reference`) in a separate
+    process: the reference's csr_omp with the system OpenMP runtime, away
+    from torch (which loads its own libgomp.so.1, already started unbound),
+    so the CPU baseline and the reference arm are the same measurement."""
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "OMP_PROC_BIND")}
+    out = subprocess.run([sys.executable, os.path.abspath(__file__), "--impl", "reference", "--steps", str(steps),
+                          "--warmup", "3"], capture_output=True, text=True, timeout=600, env=env)
+    line = next((ln for ln in out.stdout.splitlines() if ln.startswith("{")), None)
+    if out.returncode != 0 or line is None:
+        return {"unavailable": (out.stderr or out.stdout)[-300:]}
+    d = json.loads(line)
+    cpu = dict(d["cpu_baseline"])
+    cpu["process"] = "separate process without torch: the same command as the reference arm"
+    return cpu
 
 
 def spmv_bytes(m, n, nnz, vbytes=8, ibytes=4, ybytes=8):
@@ -220,13 +238,10 @@ class ClockSampler:
 # ------------------------------------------------------------------------------
 def csr_omp_runner(m, n, rowptr, colind, values, x, threads):
     """A callable running csr_omp once: the reference's own code when
-    oracle/_ref was built (its copy of the matrix first touched by the same
-    threads in csr_omp's row schedule, so on a host with several memory
-    nodes each thread reads local memory), else the C restatement; and its
-    kind."""
+    oracle/_ref was built, else the C restatement; and its kind."""
     import oracle
     if oracle.ref_available():
-        R = oracle.RefCsr(m, n, rowptr, colind, values, place_threads=threads)
+        R = oracle.RefCsr(m, n, rowptr, colind, values)
         y = np.empty(m)
         return (lambda: R.spmv(x, np.float64, threads, out=y)), "reference"  # noqa: E731
     return (lambda: oracle.spmv_csr(m, rowptr, colind, values, x, np.float64, threads)), "port"  # noqa: E731
@@ -405,7 +420,9 @@ def workload_sweep(torch, S, ctx, stream, A2, peak, flush, log):
         def launch_pick(i, s):
             M.spmv(x, y, kernel=pk[1], lanes=pk[2], block=pk[3], stream=s)
         cold = event_time_ms(torch, stream, launch_pick, 10, 3, flush=flush)
-        ours_ref_protocol = event_time_ms(torch, stream, launch_pick, 20, 5)
+        # The reference's SpmvRunner::run protocol, run in C++ by the library.
+        ours_ref_protocol = M.spmv_time(x, y, kernel=pk[1], lanes=pk[2], block=pk[3], iters=20, warmup=5,
+                                        stream=stream)["median_ms"]
         entry = {
             "m": A.m, "n": A.n, "nnz": A.nnz, "dtype": dt, "pick": pick_label, "rule": choice["reason"],
             "us": {k: round(v * 1e3, 2) for k, v in times.items()}, "unavailable": skipped or None,
@@ -431,7 +448,7 @@ def workload_sweep(torch, S, ctx, stream, A2, peak, flush, log):
                 "ours_pick_same_protocol_us": ours_ref_protocol * 1e3,
                 "speedup_vs_best": ref_t[best] / ours_ref_protocol,
                 "protocol": "reference SpmvRunner::run: one event pair per launch, median of 20 after 5 warm-up; "
-                            "ours timed the same way"}
+                            "ours by the same C++ loop (spmvb_spmv_time)"}
         M.close()
         del x, y
         out[name] = entry
@@ -766,13 +783,7 @@ def main():
             workloads = workload_sweep(torch, S, ctx, stream, A, peak, flush, log)
             del flush
         if not args.no_cpu_baseline:
-            prepare_cpu_run()
-            run, kind = csr_omp_runner(A.m, A.n, A.rowptr, A.colind, A.values, xh, host_threads())
-            cms, cmean, runs = time_csr_omp(run, 3, budget_s=10.0)
-            cpu = {"value": 2.0 * A.nnz / (cms * 1e-3) / 1e9, "unit": "GFLOP/s", "cores": host_threads(),
-                   "kind": kind, "omp_proc_bind": os.environ.get("OMP_PROC_BIND"),
-                   "sample": f"full {WORKLOAD} csr_omp SpMV: 3 warm-up runs, then the median of {runs} runs "
-                             "(the reference bench's CPU protocol)"}
+            cpu = cpu_baseline_in_clean_process(400)
 
     if rank == 0:
         full_traffic = profiled_traffic(kname)

@@ -220,6 +220,17 @@ spmvb_status spmvb_spmv_host(spmvb_matrix A, spmvb_kernel kernel, int lanes,
                              int block, const void* h_x, void* h_y,
                              spmvb_dtype acc, void* stream);
 
+/* The measurement of SpmvRunner::run (src/cuda/spmv_cuda.cu:466-486):
+ * `warmup` launches, a synchronize, then `iters` launches each between its
+ * own pair of events on `stream`, each waited for. out_ms4 receives the
+ * median, mean, min and max milliseconds (the reference's summarize,
+ * include/spmvbench/timer.hpp). The launches and the timing run in C++, so
+ * a caller from any language gets the reference's protocol. */
+spmvb_status spmvb_spmv_time(spmvb_matrix A, spmvb_kernel kernel, int lanes,
+                             int block, const void* d_x, void* d_y,
+                             spmvb_dtype acc, int iters, int warmup,
+                             void* stream, double* out_ms4);
+
 /* Merge-path y = A x that allocates nothing. No counterpart in the reference.
  * For callers that cannot call cudaMalloc: device memory owned by another
  * allocator (a caching allocator or a pool sized at start-up), or latency

@@ -90,8 +90,6 @@ def ref() -> C.CDLL:
             getattr(lib, f"ref_csr_create_{t}").argtypes = [C.c_int32, C.c_int32, C.c_int64, P, P, ct]
             getattr(lib, f"ref_csr_create_{t}").restype = P
             getattr(lib, f"ref_csr_destroy_{t}").argtypes = [P]
-        lib.ref_csr_create_placed_d.argtypes = [C.c_int32, C.c_int32, C.c_int64, P, P, P, C.c_int]
-        lib.ref_csr_create_placed_d.restype = P
         for suf in ("dd", "ff", "fd"):
             getattr(lib, f"ref_spmv_csr_{suf}").argtypes = [P, P, P, C.c_int]
             getattr(lib, f"ref_spmm_csr_{suf}").argtypes = [P, P, P, C.c_int, C.c_int]
@@ -329,18 +327,12 @@ def generate_vector(seed: int, n: int) -> np.ndarray:
 class RefCsr:
     """A CsrMatrix<T> owned by the reference library."""
 
-    def __init__(self, m, n, rowptr, colind, vals, place_threads=0):
-        """place_threads > 0 (fp64): the reference's copy of the arrays is
-        first touched by that many OpenMP threads in csr_omp's static row
-        schedule, so each thread's rows sit in its own memory node."""
+    def __init__(self, m, n, rowptr, colind, vals):
         self.lib = ref()
         self.t = "d" if vals.dtype == np.float64 else "f"
         self._keep = (rowptr, colind, vals)
-        nnz = int(rowptr[m]) if m else 0
-        if place_threads > 0 and self.t == "d":
-            self.h = self.lib.ref_csr_create_placed_d(m, n, nnz, _p(rowptr), _p(colind), _p(vals), place_threads)
-        else:
-            self.h = getattr(self.lib, f"ref_csr_create_{self.t}")(m, n, nnz, _p(rowptr), _p(colind), _p(vals))
+        self.h = getattr(self.lib, f"ref_csr_create_{self.t}")(m, n, int(rowptr[m]) if m else 0,
+                                                               _p(rowptr), _p(colind), _p(vals))
         self.m, self.n, self.vdtype = m, n, vals.dtype
 
     def close(self):

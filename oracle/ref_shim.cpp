@@ -12,10 +12,6 @@
 #include <string>
 #include <vector>
 
-#ifdef _OPENMP
-#include <omp.h>
-#endif
-
 #include "spmvbench/bcsr.hpp"
 #include "spmvbench/csr.hpp"
 #include "spmvbench/ell.hpp"
@@ -27,38 +23,12 @@
 namespace R = spmvbench;
 
 namespace {
-// The reference's CsrMatrix holding a copy of the arrays. With nt > 0 the
-// fresh (untouched) storage is first written by nt OpenMP threads with the
-// static row schedule of spmv_csr_cpu (src/cpu/spmv_cpu.cpp:15-26), so on a
-// host with several memory nodes each thread's rows sit in its own node's
-// memory when the timed products run, as a NUMA-aware caller would place
-// them; the copy that follows only rewrites the same pages.
 template <typename T>
-R::CsrMatrix<T>* make(int32_t m, int32_t n, int64_t nnz, const int32_t* rp, const int32_t* ci, const T* v,
-                      int nt = 0) {
+R::CsrMatrix<T>* make(int32_t m, int32_t n, int64_t nnz, const int32_t* rp, const int32_t* ci, const T* v) {
   auto* A = new R::CsrMatrix<T>();
   A->m = m;
   A->n = n;
   A->nnz = nnz;
-#ifdef _OPENMP
-  if (nt > 0 && m > 0) {
-    A->rowptr.reserve(static_cast<size_t>(m) + 1);
-    A->colind.reserve(static_cast<size_t>(nnz));
-    A->values.reserve(static_cast<size_t>(nnz));
-    int32_t* prp = A->rowptr.data();
-    int32_t* pci = A->colind.data();
-    T* pv = A->values.data();
-    omp_set_num_threads(nt);
-#pragma omp parallel for schedule(static)
-    for (int32_t i = 0; i < m; ++i) {
-      prp[i] = rp[i];
-      for (int32_t p = rp[i]; p < rp[i + 1]; ++p) {
-        pci[p] = ci[p];
-        pv[p] = v[p];
-      }
-    }
-  }
-#endif
   A->rowptr.assign(rp, rp + m + 1);
   A->colind.assign(ci, ci + nnz);
   A->values.assign(v, v + nnz);
@@ -73,12 +43,6 @@ void* ref_csr_create_d(int32_t m, int32_t n, int64_t nnz, const int32_t* rp, con
 }
 void* ref_csr_create_f(int32_t m, int32_t n, int64_t nnz, const int32_t* rp, const int32_t* ci, const float* v) {
   return make<float>(m, n, nnz, rp, ci, v);
-}
-// Same, with the storage first touched by `nt` threads in spmv_csr_cpu's row
-// schedule (see make).
-void* ref_csr_create_placed_d(int32_t m, int32_t n, int64_t nnz, const int32_t* rp, const int32_t* ci,
-                              const double* v, int nt) {
-  return make<double>(m, n, nnz, rp, ci, v, nt);
 }
 void ref_csr_destroy_d(void* h) { delete static_cast<R::CsrMatrix<double>*>(h); }
 void ref_csr_destroy_f(void* h) { delete static_cast<R::CsrMatrix<float>*>(h); }

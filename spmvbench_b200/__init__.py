@@ -363,6 +363,16 @@ class DeviceMatrix:
         1 = one row-order pass); bit-identical results either way."""
         call("spmvb_matrix_set_spmm_bands", self.handle, bands)
 
+    def spmv_time(self, x, y, kernel: int = CSR_SCALAR, lanes: int = 4, block: int = 4, iters: int = 20,
+                  warmup: int = 5, acc: int | None = None, stream=None) -> dict:
+        """SpmvRunner::run's measurement in C++ (spmvb_spmv_time): median /
+        mean / min / max ms of `iters` launches, one event pair each."""
+        acc = self.dtype if acc is None else acc
+        out = np.zeros(4)
+        call("spmvb_spmv_time", self.handle, kernel, lanes, block, C.c_void_p(x.data_ptr()),
+             C.c_void_p(y.data_ptr()), acc, iters, warmup, _stream_ptr(stream), _ptr(out))
+        return dict(zip(("median_ms", "mean_ms", "min_ms", "max_ms"), out.tolist()))
+
     def spmm(self, X, Y, k: int, tile: int = 32, bucketed: bool = False,
              acc: int | None = None, stream=None) -> None:
         acc = self.dtype if acc is None else acc

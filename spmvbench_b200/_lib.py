@@ -92,6 +92,7 @@ SIGNATURES = {
     "spmvb_matrix_export_bcsr": (C.c_int, [P, C.c_int, P, P, P]),
     "spmvb_spmv": (C.c_int, [P, C.c_int, C.c_int, C.c_int, P, P, C.c_int, P]),
     "spmvb_spmv_host": (C.c_int, [P, C.c_int, C.c_int, C.c_int, P, P, C.c_int, P]),
+    "spmvb_spmv_time": (C.c_int, [P, C.c_int, C.c_int, C.c_int, P, P, C.c_int, C.c_int, C.c_int, P, P]),
     "spmvb_spmv_merge_noalloc": (C.c_int, [C.c_int, C.c_int32, C.c_int32, C.c_int64, P, P, P, P, P,
                                            C.c_int, P]),
     "spmvb_spmm": (C.c_int, [P, C.c_int, C.c_int, C.c_int, P, P, C.c_int, P]),

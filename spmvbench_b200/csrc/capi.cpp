@@ -438,6 +438,51 @@ spmvb_status spmvb_spmv(spmvb_matrix A, spmvb_kernel kernel, int lanes, int bloc
   return dispatch_spmv(A, kernel, lanes, block, d_x, d_y, acc, static_cast<cudaStream_t>(stream));
 }
 
+spmvb_status spmvb_spmv_time(spmvb_matrix A, spmvb_kernel kernel, int lanes, int block, const void* d_x, void* d_y,
+                             spmvb_dtype acc, int iters, int warmup, void* stream, double* out_ms4) {
+  clear_error();
+  if (!out_ms4 || iters < 1 || warmup < 0) return fail(SPMVB_ERR_INVALID_ARGUMENT, "bad timing arguments");
+  SPMVB_TRY(check_pair(A, acc));
+  if (kernel < 0 || kernel >= SPMVB_KERNEL_COUNT) return fail(SPMVB_ERR_INVALID_ARGUMENT, "unknown kernel id");
+  DeviceGuard g(A->device);
+  SPMVB_TRY(check_device_ptr(d_x, size_t(A->n) * dtype_size(A->dtype), A->device, "x"));
+  SPMVB_TRY(check_device_ptr(d_y, size_t(A->m) * dtype_size(acc), A->device, "y"));
+  SPMVB_TRY(spmvb_matrix_prepare(A, kernel, kernel == SPMVB_BCSR ? (block <= 2 ? 2 : 4) : 0));
+  auto s = static_cast<cudaStream_t>(stream);
+  for (int i = 0; i < warmup; ++i) SPMVB_TRY(dispatch_spmv(A, kernel, lanes, block, d_x, d_y, acc, s));
+  SPMVB_TRY_CUDA(cudaStreamSynchronize(s));
+  struct Ev {
+    cudaEvent_t a = nullptr, b = nullptr;
+    ~Ev() {
+      if (a) cudaEventDestroy(a);
+      if (b) cudaEventDestroy(b);
+    }
+  } ev;
+  SPMVB_TRY_CUDA(cudaEventCreate(&ev.a));
+  SPMVB_TRY_CUDA(cudaEventCreate(&ev.b));
+  std::vector<double> t(static_cast<size_t>(iters));
+  for (int i = 0; i < iters; ++i) {
+    SPMVB_TRY_CUDA(cudaEventRecord(ev.a, s));
+    SPMVB_TRY(dispatch_spmv(A, kernel, lanes, block, d_x, d_y, acc, s));
+    SPMVB_TRY_CUDA(cudaEventRecord(ev.b, s));
+    SPMVB_TRY_CUDA(cudaEventSynchronize(ev.b));
+    float ms = 0.f;
+    SPMVB_TRY_CUDA(cudaEventElapsedTime(&ms, ev.a, ev.b));
+    t[static_cast<size_t>(i)] = ms;
+  }
+  SPMVB_TRY(check_err_word(A->ctx, s));
+  std::vector<double> sorted = t;
+  std::sort(sorted.begin(), sorted.end());
+  const size_t n = sorted.size();
+  out_ms4[0] = n % 2 ? sorted[n / 2] : 0.5 * (sorted[n / 2 - 1] + sorted[n / 2]);
+  double sum = 0.0;
+  for (double v : t) sum += v;
+  out_ms4[1] = sum / static_cast<double>(n);
+  out_ms4[2] = sorted.front();
+  out_ms4[3] = sorted.back();
+  return SPMVB_OK;
+}
+
 spmvb_status spmvb_spmv_host(spmvb_matrix A, spmvb_kernel kernel, int lanes, int block, const void* h_x, void* h_y,
                              spmvb_dtype acc, void* stream) {
   clear_error();

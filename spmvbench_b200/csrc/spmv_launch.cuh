@@ -123,7 +123,9 @@ spmvb_status launch_spmv(spmvb_matrix A, spmvb_kernel kernel, int lanes,
         else if (stages == 4) SPMVB_TRY((launch_ell_tma<T, Acc, kEllTmaMaxWidth, 4>(A, e, x, y, stream)));
         else SPMVB_TRY((launch_ell_tma<T, Acc, kEllTmaMaxWidth, 3>(A, e, x, y, stream)));
       } else {
-        ell_rows<T, Acc, false><<<(A->m + kRowThreads - 1) / kRowThreads, kRowThreads, 0, stream>>>(e, x, y);
+        const char* ct = std::getenv("SPMVB_ELL_CTA");
+        const int cta = ct ? std::atoi(ct) : kRowThreads;
+        ell_rows<T, Acc, false><<<(A->m + cta - 1) / cta, cta, 0, stream>>>(e, x, y);
       }
       count_launch();
       break;

@@ -290,3 +290,20 @@ def test_rank_that_never_joins_times_out(tmp_path):
     out = subprocess.run([sys.executable, "-c", _NEVER_JOINS], env=env, capture_output=True, text=True,
                          timeout=120)
     assert "STATUS 7" in out.stdout, out.stdout + out.stderr
+
+
+def test_spmv_time_is_the_reference_protocol(ctx):
+    """spmvb_spmv_time: SpmvRunner::run's measurement in C++ (warm-up, one
+    event pair per launch, median/mean/min/max); y is the kernel's result."""
+    A = S.generate(2, seed=88, scale_rows=50000)
+    xh = S.generate_vector(89, A.n)
+    M = S.DeviceMatrix(ctx, A, S.F64)
+    x = torch.from_numpy(xh).cuda()
+    y = torch.full((A.m,), float("nan"), dtype=torch.float64, device="cuda")
+    t = M.spmv_time(x, y, kernel=S.ELL, iters=9, warmup=2)
+    assert 0 < t["min_ms"] <= t["median_ms"] <= t["max_ms"] and t["min_ms"] <= t["mean_ms"] <= t["max_ms"]
+    torch.cuda.synchronize()
+    assert_bitwise(oracle_y(A, xh, S.F64, S.F64), y.cpu().numpy(), "timed launches")
+    with pytest.raises(S.SpmvbError):
+        M.spmv_time(x, y, kernel=S.ELL, iters=0)
+    M.close()
