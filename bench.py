@@ -263,6 +263,30 @@ def time_csr_omp(run, warmup, runs=None, budget_s=None, min_runs=10):
     return statistics.median(times), statistics.fmean(times), len(times)
 
 
+def host_state() -> dict:
+    """What can make the same CPU run differ between two moments on one host:
+    transparent huge pages (mode, and how much of this process they back),
+    load average, and the cores' current clock (median over /proc/cpuinfo)."""
+    st = {}
+    try:
+        st["thp"] = open("/sys/kernel/mm/transparent_hugepage/enabled").read().strip()
+    except OSError:
+        pass
+    try:
+        for ln in open("/proc/self/smaps_rollup"):
+            if ln.startswith("AnonHugePages:"):
+                st["anon_huge_kb"] = int(ln.split()[1])
+    except OSError:
+        pass
+    try:
+        st["loadavg"] = open("/proc/loadavg").read().split()[:3]
+        mhz = [float(ln.split(":")[1]) for ln in open("/proc/cpuinfo") if ln.startswith("cpu MHz")]
+        st["cpu_mhz_median"] = statistics.median(mhz) if mhz else None
+    except (OSError, ValueError):
+        pass
+    return st
+
+
 def run_reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -282,7 +306,7 @@ def run_reference_arm(args):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
         "config": bench_config(args.gpus, "csr_omp (spmv_csr_cpu, OpenMP static)"),
         "cpu_baseline": {"value": gflops, "unit": "GFLOP/s", "cores": threads, "kind": kind,
-                         "omp_proc_bind": os.environ.get("OMP_PROC_BIND"),
+                         "omp_proc_bind": os.environ.get("OMP_PROC_BIND"), "host": host_state(),
                          "sample": f"full {WORKLOAD} SpMV per step: {warm} warm-up runs, then the median of "
                                    f"{runs} timed runs (the reference bench's CPU protocol)"},
         "e2e": {"value": gflops, "unit": "GFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

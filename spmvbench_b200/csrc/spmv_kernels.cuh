@@ -666,4 +666,74 @@ __global__ void __launch_bounds__(256)
   if (gi < B.m) y[gi] = acc;
 }
 
+// ---------------------------------------------------------------------------
+// BCSR 4x4, fp64, on the tensor cores (an experiment; SPMVB_BCSR_MMA=1 selects
+// it, bcsr_rows is the default). sm_100's fp64 tensor path is the warp-level
+// mma.sync m8n8k4 (tcgen05 has no f64 kind). A warp owns block rows P = 2q
+// and Q = 2q + 1 and walks their blocks pairwise: A (8 x 4) stacks the j-th
+// block of P (rows 0-3) over the j-th block of Q (rows 4-7); B (4 x 8) holds
+// P's x slice in column 0 and Q's in column 1 (zeros elsewhere); D
+// accumulates over j, and D[0..3][0], D[4..7][1] are the two block rows' y -
+// 8 useful outputs of the 64 each MMA computes, since every block meets its
+// own x slice. The tensor core adds each block's four products in its own
+// order, so y is within the gamma_n bound of spmv_bcsr_cpu, not bit-identical.
+// Fragments (PTX m8n8k4 .f64): lane l holds A[l/4][l%4], B[l%4][l/4] and
+// D[l/4][2*(l%4) + {0,1}].
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void dmma_8x8x4(double (&d)[2], double a, double b) {
+  asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
+               : "+d"(d[0]), "+d"(d[1])
+               : "d"(a), "d"(b));
+}
+
+// UB: block pairs whose fragments are loaded before their MMAs.
+template <int UB>
+__global__ void __launch_bounds__(256) bcsr4_dmma(BcsrView B, const double* __restrict__ x, double* __restrict__ y) {
+  const double* __restrict__ vals = static_cast<const double*>(B.values);
+  const uint64_t ps = policy_evict_first();
+  const uint64_t pk = policy_evict_last();
+  const int lane = threadIdx.x & (kWarp - 1);
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / kWarp;
+  const int64_t P = warp * 2;
+  if (P >= B.mb) return;
+  const bool hasQ = P + 1 < B.mb;
+  const int r = lane >> 2;  // A row / B column of this lane
+  const int k = lane & 3;   // A column / B row of this lane
+  const int sP = B.rowptr[P], eP = B.rowptr[P + 1];
+  const int sQ = hasQ ? B.rowptr[P + 1] : 0, eQ = hasQ ? B.rowptr[P + 2] : 0;
+  const int len = max(eP - sP, eQ - sQ);
+  const bool mine_P = r < 4;
+  double d[2] = {0.0, 0.0};
+  for (int j0 = 0; j0 < len; j0 += UB) {
+    double a[UB], b[UB];
+#pragma unroll
+    for (int u = 0; u < UB; ++u) {
+      const int j = j0 + u;
+      const int pP = sP + j, pQ = sQ + j;
+      // A: this lane's element of the j-th block of P (rows 0-3) or Q (4-7).
+      const int pa = mine_P ? pP : pQ;
+      const bool va = mine_P ? (pP < eP) : (pQ < eQ);
+      a[u] = va ? ld_stream(vals + static_cast<int64_t>(pa) * 16 + (r & 3) * 4 + k, ps) : 0.0;
+      // B: column 0 = P's x slice, column 1 = Q's; lane holds B[k][r].
+      double bv = 0.0;
+      if (r == 0 && pP < eP) {
+        const int gc = ld_stream(B.colind + pP, ps) * 4 + k;
+        if (gc < B.n) bv = ld_keep(x + gc, pk);
+      } else if (r == 1 && pQ < eQ) {
+        const int gc = ld_stream(B.colind + pQ, ps) * 4 + k;
+        if (gc < B.n) bv = ld_keep(x + gc, pk);
+      }
+      b[u] = bv;
+    }
+#pragma unroll
+    for (int u = 0; u < UB; ++u) dmma_8x8x4(d, a[u], b[u]);
+  }
+  // D[r][0] for r < 4 (block row P) and D[r][1] for r >= 4 (block row Q)
+  // sit in the lanes with k == 0.
+  if (k == 0) {
+    const int64_t gi = mine_P ? P * 4 + r : (P + 1) * 4 + (r - 4);
+    if (gi < B.m && (mine_P || hasQ)) y[gi] = mine_P ? d[0] : d[1];
+  }
+}
+
 }  // namespace spmvb

@@ -6,6 +6,7 @@
 #include <algorithm>
 
 #include <cstdlib>
+#include <type_traits>
 
 #include "ell_tma.cuh"
 #include "internal.hpp"
@@ -15,6 +16,8 @@
 namespace spmvb {
 
 constexpr int kRowThreads = 256;
+// Threads per CTA of ell_rows (see its launch).
+constexpr int kEllThreads = 64;
 // BCSR: blocks requested per batch per thread.
 constexpr int kBcsrBatch = 2;
 // Warp-staged scalar kernel: entries per warp chunk.
@@ -27,6 +30,13 @@ static void launch_vector(const CsrView& v, int sms, const T* x, Acc* y,
   const int64_t need = (v.m + rows_per_block - 1) / rows_per_block;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(need, int64_t(sms) * 16)));
   csr_vector<T, Acc, G><<<grid, kRowThreads, 0, s>>>(v, x, y);
+}
+
+// SPMVB_BCSR_MMA=1: fp64 BCSR 4x4 on the tensor cores (bcsr4_dmma), an
+// experiment measured against bcsr_rows.
+static bool bcsr_mma_requested() {
+  const char* e = std::getenv("SPMVB_BCSR_MMA");
+  return e && *e == '1';
 }
 
 // ELL widths ell_tma serves (wider matrices run ell_rows).
@@ -123,9 +133,11 @@ spmvb_status launch_spmv(spmvb_matrix A, spmvb_kernel kernel, int lanes,
         else if (stages == 4) SPMVB_TRY((launch_ell_tma<T, Acc, kEllTmaMaxWidth, 4>(A, e, x, y, stream)));
         else SPMVB_TRY((launch_ell_tma<T, Acc, kEllTmaMaxWidth, 3>(A, e, x, y, stream)));
       } else {
-        const char* ct = std::getenv("SPMVB_ELL_CTA");
-        const int cta = ct ? std::atoi(ct) : kRowThreads;
-        ell_rows<T, Acc, false><<<(A->m + cta - 1) / cta, cta, 0, stream>>>(e, x, y);
+        // 64-thread CTAs: a row block that fills less than one wave (an
+        // 8-way shard of 1M rows: 125k rows) spreads over the SMs within 2 %
+        // instead of the 21 % that 256-thread CTAs leave (measured 11.4 us
+        // against 12.6 us; no change at 1M rows).
+        ell_rows<T, Acc, false><<<(A->m + kEllThreads - 1) / kEllThreads, kEllThreads, 0, stream>>>(e, x, y);
       }
       count_launch();
       break;
@@ -188,6 +200,11 @@ spmvb_status launch_spmv(spmvb_matrix A, spmvb_kernel kernel, int lanes,
       if (bs == 2) {
         if (vec_x) bcsr_rows<T, Acc, 2, 2, true, kBcsrBatch><<<grid, kRowThreads, 0, stream>>>(bv, x, y);
         else bcsr_rows<T, Acc, 2, 2, false, kBcsrBatch><<<grid, kRowThreads, 0, stream>>>(bv, x, y);
+      } else if (std::is_same<T, double>::value && std::is_same<Acc, double>::value && bcsr_mma_requested()) {
+        // Tensor-core experiment (bcsr4_dmma): a warp per pair of block rows.
+        const int64_t warps = (int64_t(b.mb) + 1) / 2;
+        const int g = static_cast<int>(std::max<int64_t>(1, (warps * kWarp + kRowThreads - 1) / kRowThreads));
+        bcsr4_dmma<4><<<g, kRowThreads, 0, stream>>>(bv, reinterpret_cast<const double*>(x), reinterpret_cast<double*>(y));
       } else {
         if (vec_x) bcsr_rows<T, Acc, 4, 4, true, kBcsrBatch><<<grid, kRowThreads, 0, stream>>>(bv, x, y);
         else bcsr_rows<T, Acc, 4, 4, false, kBcsrBatch><<<grid, kRowThreads, 0, stream>>>(bv, x, y);

@@ -307,6 +307,22 @@ def _adversarial_csr(rng):
     return S.CsrMatrix(m, n, rowptr, colind, rng.uniform(-1, 1, nnz))
 
 
+def _distinct_columns(A):
+    """A with each row's repeated columns dropped (first kept), order kept."""
+    rows_c, rows_v = [], []
+    for i in range(A.m):
+        c = A.colind[A.rowptr[i]:A.rowptr[i + 1]]
+        _, first = np.unique(c, return_index=True)
+        keep = np.sort(first)
+        rows_c.append(c[keep])
+        rows_v.append(A.values[A.rowptr[i]:A.rowptr[i + 1]][keep])
+    rp = np.zeros(A.m + 1, np.int32)
+    rp[1:] = np.cumsum([r.size for r in rows_c])
+    ci = np.concatenate(rows_c).astype(np.int32) if A.m else np.zeros(0, np.int32)
+    va = np.concatenate(rows_v) if A.m else np.zeros(0)
+    return S.CsrMatrix(A.m, A.n, rp, ci, va)
+
+
 def test_device_bcsr_and_row_stats_on_adversarial_matrices(ctx):
     """The on-device BCSR conversion (one stable radix sort of block keys) and
     the device block census of row statistics on 120 adversarial matrices:
@@ -362,3 +378,26 @@ def test_ell_tma_stream_is_bit_identical(ctx, monkeypatch, which, rows, stages):
         assert_bitwise(oracle_y(A, x, dt, acc), run_spmv(M, x, S.ELL, acc=acc), f"ell tma {dt}/{acc}")
         M.close()
     ctx.check()  # no bounded wait gave up
+
+
+@pytest.mark.parametrize("which,rows", [(4, 40000), (4, 40004), (1, 0), (1, 1001), (2, 30000)])
+def test_bcsr_tensor_core_experiment_within_gamma(ctx, monkeypatch, which, rows):
+    """BCSR 4x4 on the fp64 tensor cores (SPMVB_BCSR_MMA=1, mma.sync m8n8k4,
+    two block rows per warp): within the gamma_n bound of csr_omp, including
+    an odd number of block rows (the last warp has no second block row), a
+    last block row cut by m, and a last block column cut by n."""
+    monkeypatch.setenv("SPMVB_BCSR_MMA", "1")
+    A = S.generate(which, seed=59, scale_rows=rows)
+    x = mixed_x(A.n, seed=60)
+    M = S.DeviceMatrix(ctx, A, S.F64)
+    got = run_spmv(M, x, S.BCSR, block=4)
+    assert_rows_within_bound(A, x, oracle_y(A, x, S.F64, S.F64), got, S.F64, S.F64, "bcsr dmma")
+    M.close()
+    rng = np.random.default_rng(61)
+    for t in range(20):
+        C = _distinct_columns(_adversarial_csr(rng))  # repeated entries: BCSR keeps the last one
+        xc = rng.uniform(-1, 1, C.n)
+        MC = S.DeviceMatrix(ctx, C, S.F64)
+        assert_rows_within_bound(C, xc, oracle_y(C, xc, S.F64, S.F64), run_spmv(MC, xc, S.BCSR, block=4),
+                                 S.F64, S.F64, f"bcsr dmma adversarial {t}")
+        MC.close()
