@@ -18,7 +18,9 @@
 //
 //   ell_rows_peer  one launch per step: ELL rows (same order as ell_rows, so
 //                  bit-identical to csr_omp), each row's sum stored to every
-//                  rank, barrier.
+//                  rank, barrier. SPMVB_PEER_ROWS_PER_THREAD deals each thread
+//                  several rows in turn; SPMVB_PEER_CTA_FENCE=1 makes every
+//                  CTA fence its own stores at system scope before arriving.
 //   peer_push      after a non-fused SpMV: copy the local slice to every
 //                  rank, barrier.
 //   peer_barrier   barrier only.
@@ -81,9 +83,14 @@ __device__ bool peer_wait_all(const PeerView& P, unsigned long long phase) {
 }
 
 // All threads of every CTA, after the CTA's last store: the barrier above.
+// With P.cta_fence, each CTA first makes its own stores visible at system
+// scope (the barrier orders the CTA's threads before thread 0's fence, which
+// covers what thread 0 has observed), so the remote stores drain while other
+// CTAs still compute and the last CTA's fence only waits for its own.
 __device__ void peer_arrive(const PeerView& P) {
   __syncthreads();
   if (threadIdx.x == 0) {
+    if (P.cta_fence) __threadfence_system();
     unsigned prev;
     asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(P.counter) : "memory");
     if (prev == gridDim.x - 1) {
@@ -164,6 +171,14 @@ static int peer_grid(int rows, int sm_count, int rows_per_thread = 1) {
   return std::max(1, std::min((rows + 256 * per - 1) / (256 * per), sm_count * 8));
 }
 
+static bool peer_cta_fence() {
+  static const bool v = [] {
+    const char* e = std::getenv("SPMVB_PEER_CTA_FENCE");
+    return e && *e == '1';
+  }();
+  return v;
+}
+
 static int peer_rows_per_thread() {
   static const int v = [] {
     const char* e = std::getenv("SPMVB_PEER_ROWS_PER_THREAD");
@@ -184,10 +199,12 @@ spmvb_status peer_launch_ell(spmvb_matrix A, const PeerView& P, const void* x, c
   e.width = A->ell_width;
   e.ld = A->m;
   const int grid = peer_grid(A->m, A->ctx->sm_count, peer_rows_per_thread());
+  PeerView V = P;
+  V.cta_fence = peer_cta_fence() ? 1 : 0;
   if (A->dtype == SPMVB_F64)
-    ell_rows_peer<double><<<grid, kPeerRowThreads, 0, s>>>(e, static_cast<const double*>(x), P);
+    ell_rows_peer<double><<<grid, kPeerRowThreads, 0, s>>>(e, static_cast<const double*>(x), V);
   else
-    ell_rows_peer<float><<<grid, kPeerRowThreads, 0, s>>>(e, static_cast<const float*>(x), P);
+    ell_rows_peer<float><<<grid, kPeerRowThreads, 0, s>>>(e, static_cast<const float*>(x), V);
   count_launch();
   SPMVB_TRY_CUDA(cudaGetLastError());
   return SPMVB_OK;
@@ -195,10 +212,12 @@ spmvb_status peer_launch_ell(spmvb_matrix A, const PeerView& P, const void* x, c
 
 spmvb_status peer_launch_push(spmvb_dtype dtype, const void* y, const PeerView& P, int sm_count, cudaStream_t s) {
   const int grid = peer_grid(P.rows, sm_count);
+  PeerView V = P;
+  V.cta_fence = peer_cta_fence() ? 1 : 0;
   if (dtype == SPMVB_F64)
-    peer_push<double><<<grid, 256, 0, s>>>(static_cast<const double*>(y), P);
+    peer_push<double><<<grid, 256, 0, s>>>(static_cast<const double*>(y), V);
   else
-    peer_push<float><<<grid, 256, 0, s>>>(static_cast<const float*>(y), P);
+    peer_push<float><<<grid, 256, 0, s>>>(static_cast<const float*>(y), V);
   count_launch();
   SPMVB_TRY_CUDA(cudaGetLastError());
   return SPMVB_OK;

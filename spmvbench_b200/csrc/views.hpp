@@ -133,6 +133,7 @@ struct PeerView {
   int nranks = 1;
   int rank = 0;
   int rows = 0;
+  int cta_fence = 0;  // every CTA fences its own stores before arriving
 };
 
 }  // namespace spmvb
