@@ -4,8 +4,8 @@ compare with the oracle.
 Tolerance (stated once, used everywhere): a row passes when
     |y_gpu - y_ref| <= max(tol * |y_ref|, 2 * gamma_n(u) * sum_j |a_ij x_j|)
 with tol = 1e-12 (fp64 accumulation) or 1e-5 (fp32), n = the row's length,
-gamma_n = n*u / (1 - n*u), u = 2^-53 or 2^-24: the per-row relative bound of
-the north star, widened to the reference GPU test's own gamma_n criterion
+gamma_n = n*u / (1 - n*u), u = 2^-53 or 2^-24: the per-row relative bound
+set for this path, widened to the reference GPU test's own gamma_n criterion
 (tests/test_cuda_correctness.cpp:1-11,53-56,88) for rows where cancellation
 makes |y| tiny. Kernels that keep csr_omp's summation order must match
 bit for bit instead."""
