@@ -92,6 +92,19 @@ def test_spmm_full_size_fp64(ctx):
     assert_bitwise(ref, Y, "C5 full host entry")
 
 
+def test_spmm_full_size_fp32(ctx):
+    """The k = 64 SpMM workload (uniform 1M x 1M, 16 nnz/row) in fp32: Y equals
+    spmm_csr_cpu's fp32 output bit for bit, on the device and host entries."""
+    A = S.generate(5, seed=67)
+    k = 64
+    B = S.generate_vector(68, A.n * k).reshape(A.n, k).astype(np.float32)
+    M = S.DeviceMatrix(ctx, A, S.F32)
+    vals = np.ascontiguousarray(A.values, np.float32)
+    ref = oracle.spmm_csr(A.m, k, A.rowptr, A.colind, vals, B, np.float32)
+    assert_bitwise(ref, run_spmm(M, B, k, 64, False), "C5 fp32 full t=64")
+    assert_bitwise(ref, run_spmm(M, B, k, 32, False), "C5 fp32 full t=32")
+
+
 @pytest.mark.parametrize("bands", ["2", "3", "5", "8"])
 @pytest.mark.parametrize("dtype,acc", DTYPE_PAIRS)
 def test_spmm_column_band_sweep_is_bit_identical(ctx, bands, dtype, acc):

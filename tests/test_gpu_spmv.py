@@ -104,6 +104,22 @@ def test_full_size_uniform_fp64(ctx):
         assert_rows_within_bound(A, x, ref, run_spmv(M, x, k, lanes), S.F64, S.F64, S.kernel_name(k))
 
 
+@pytest.mark.parametrize("acc", [S.F32, S.F64])
+def test_full_size_uniform_fp32(ctx, acc):
+    """The uniform 1M x 1M, 16 nnz/row matrix stored in fp32: the thread-per-row
+    kernels keep csr_omp's order in the accumulator type, so they match its
+    fp32 (or fp32-in, fp64-accumulate) output bit for bit."""
+    A = S.generate(2, seed=47)
+    x = S.generate_vector(48, A.n)
+    M = S.DeviceMatrix(ctx, A, S.F32)
+    ref = oracle_y(A, x, S.F32, acc)
+    assert_bitwise(ref, run_spmv(M, x, S.CSR_SCALAR, acc=acc), f"C2 fp32/{acc} scalar")
+    assert_bitwise(ref, run_spmv(M, x, S.ELL, acc=acc), f"C2 fp32/{acc} ell")
+    for k, lanes in ((S.CSR_MERGE, 1), (S.CSR_VECTOR, 16), (S.CSR_WARP, 1), (S.HYB, 1)):
+        assert_rows_within_bound(A, x, ref, run_spmv(M, x, k, lanes, acc=acc), S.F32, acc,
+                                 f"C2 fp32/{acc} {S.kernel_name(k)}")
+
+
 def test_full_size_powerlaw_fp64(ctx):
     A = S.generate(3, seed=43)
     x = S.generate_vector(44, A.n)
