@@ -105,6 +105,42 @@ def test_spmm_full_size_fp32(ctx):
     assert_bitwise(ref, run_spmm(M, B, k, 32, False), "C5 fp32 full t=32")
 
 
+def test_spmm_with_more_elements_than_int32(ctx):
+    """Y and X of 600,000 x 4,096 fp64 (2.46e9 elements, 19.7 GB each): the
+    element offsets row * k pass 2^31 from row 524,288 on, so X and Y are
+    addressed with 64-bit offsets. X is built on the device from exact
+    binary fractions; the last 2,000 rows of Y equal spmm_csr_cpu's order
+    (0 + a0*X[c0] + a1*X[c1], each step rounded) bit for bit."""
+    import torch
+    free, _ = torch.cuda.mem_get_info()
+    if free < 60e9:
+        pytest.skip("needs 60 GB of free device memory")
+    m = n = 600_000
+    k = 4096
+    rng = np.random.default_rng(73)
+    colind = np.sort(rng.integers(0, n, (m, 2), dtype=np.int32), axis=1).ravel()
+    rowptr = (np.arange(m + 1, dtype=np.int64) * 2).astype(np.int32)
+    values = rng.standard_normal(2 * m)
+    A = S.CsrMatrix(m, n, rowptr, colind, values)
+    M = S.DeviceMatrix(ctx, A, S.F64)
+    X = torch.arange(n * k, dtype=torch.float64, device="cuda").remainder_(1021).sub_(510).mul_(2.0 ** -7)
+    X = X.view(n, k)
+    Y = torch.full((m, k), float("nan"), dtype=torch.float64, device="cuda")
+    for tile in (64, 32):
+        M.spmm(X, Y, k, tile=tile, bucketed=False)
+        torch.cuda.synchronize()
+        r0 = m - 2000
+        got = Y[r0:].cpu().numpy()
+        cols = torch.from_numpy(colind[2 * r0:].astype(np.int64)).cuda()
+        xr = X.index_select(0, cols).cpu().numpy().reshape(2000, 2, k)
+        a = values[2 * r0:].reshape(2000, 2, 1)
+        ref = (np.zeros((2000, k)) + a[:, 0] * xr[:, 0]) + a[:, 1] * xr[:, 1]
+        assert_bitwise(ref, got, f"rows past 2^31 elements, tile {tile}")
+    M.close()
+    del X, Y
+    torch.cuda.empty_cache()
+
+
 @pytest.mark.parametrize("bands", ["2", "3", "5", "8"])
 @pytest.mark.parametrize("dtype,acc", DTYPE_PAIRS)
 def test_spmm_column_band_sweep_is_bit_identical(ctx, bands, dtype, acc):

@@ -149,6 +149,35 @@ def test_ell_refuses_infeasible_padding(ctx):
     assert e.value.status == 3 and "hybrid" in str(e.value)
 
 
+def test_ell_with_more_slots_than_int32(ctx):
+    """Padded ELL of 200,000 rows x an 11,000-entry row: 2.2e9 slots (26 GB),
+    past 2^31, so every slot index (builder, kernel) must be 64-bit. The
+    thread-per-row sum over each row's real entries equals csr_omp bit for
+    bit, the longest row included."""
+    import torch
+    free, _ = torch.cuda.mem_get_info()
+    if free < 40e9:
+        pytest.skip("needs 40 GB of free device memory")
+    rng = np.random.default_rng(71)
+    m = n = 200_000
+    lens = np.full(m, 4, np.int64)
+    lens[m - 7] = 11_000
+    rowptr = np.zeros(m + 1, np.int64)
+    np.cumsum(lens, out=rowptr[1:])
+    short = np.sort(rng.integers(0, n, (m, 4), dtype=np.int32), axis=1)
+    long_row = np.sort(rng.choice(n, 11_000, replace=False)).astype(np.int32)
+    colind = np.concatenate([short[:m - 7].ravel(), long_row, short[m - 6:].ravel()])
+    assert colind.size == rowptr[-1]
+    values = rng.standard_normal(rowptr[-1])
+    A = S.CsrMatrix(m, n, rowptr.astype(np.int32), colind, values)
+    x = S.generate_vector(72, n)
+    M = S.DeviceMatrix(ctx, A, S.F64)
+    M.prepare(S.ELL)
+    assert M.info()["ell_padded_nnz"] == m * 11_000 > 2**31
+    assert_bitwise(oracle_y(A, x, S.F64, S.F64), run_spmv(M, x, S.ELL), "ELL past 2^31 slots")
+    M.close()
+
+
 @pytest.mark.parametrize("which,rows", [(2, 50000), (3, 100000), (4, 20000), (1, 0)])
 def test_device_formats_match_reference_layout(ctx, which, rows):
     A = S.generate(which, seed=51, scale_rows=rows)
