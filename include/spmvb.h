@@ -56,7 +56,8 @@ typedef enum spmvb_kernel {
   SPMVB_CSR_MERGE = 3,  /* merge-path: equal (rows + nnz) share per thread   */
   SPMVB_ELL = 4,        /* column-major ELL, walks row_lengths               */
   SPMVB_BCSR = 5,       /* blocked CSR, `block` = 2 (2x2) or 4 (4x4)         */
-  SPMVB_HYB = 6,        /* ELL(K) for the first K entries + CSR tail         */
+  SPMVB_HYB = 6,        /* rows of <= K entries in ELL(K), longer rows whole
+                           in CSR streamed in chunks of <= 256 entries        */
   SPMVB_KERNEL_COUNT = 7
 } spmvb_kernel;
 
