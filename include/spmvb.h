@@ -476,8 +476,10 @@ spmvb_status spmvb_dist_get_info(spmvb_dist D, int32_t* row_begin,
  * unchanged and y unread until the call is waited for. Collective: every
  * rank submits the same sequence of calls. Pinned, mapped y is written by
  * the kernel directly (every kernel but the merge path). Runs on the NCCL
- * exchange (not after spmvb_dist_enable_peer). No reference counterpart (the
- * reference's SpmvRunner copies the whole x to its one GPU,
+ * exchange (not after spmvb_dist_enable_peer). Destroying the dist handle
+ * first waits for the pipeline's calls; the pipeline's later calls then fail
+ * and only its destroy remains valid. No reference counterpart (the reference's
+ * SpmvRunner copies the whole x to its one GPU,
  * src/cuda/spmv_cuda.cu:292-330). */
 typedef struct spmvb_dist_pipeline_st* spmvb_dist_pipeline;
 spmvb_status spmvb_dist_pipeline_create(spmvb_dist D, int depth,

@@ -70,6 +70,9 @@ struct spmvb_dist_st {
   };
   std::vector<Graph> graphs;
   cudaStream_t capture = nullptr;
+  // Host-buffer pipelines made on this handle: their work drains before the
+  // communicator and the matrix go.
+  std::vector<spmvb_dist_pipeline_st*> pipelines;
 
   void close_peers() {
     for (int q = 0; q < kMaxRanks; ++q)
@@ -266,6 +269,8 @@ spmvb_status spmvb_dist_create(spmvb_context ctx, int nranks, int rank, const vo
   return SPMVB_OK;
 }
 
+static void detach_pipeline(spmvb_dist_pipeline_st* P);
+
 spmvb_status spmvb_dist_destroy(spmvb_dist D) {
   clear_error();
   if (!D) return SPMVB_OK;
@@ -284,6 +289,8 @@ spmvb_status spmvb_dist_destroy(spmvb_dist D) {
   // Graphs that hold NCCL calls go before the communicator does.
   for (auto& gr : D->graphs) cudaGraphExecDestroy(gr.exec);
   D->graphs.clear();
+  for (auto* P : D->pipelines) detach_pipeline(P);
+  D->pipelines.clear();
   if (D->comm) {
     ncclCommFinalize(D->comm);
     nccl_wait(D->comm, 30.0, "ncclCommFinalize");
@@ -692,7 +699,8 @@ spmvb_status spmvb_dist_get_info(spmvb_dist D, int32_t* row_begin, int32_t* row_
 // communication stream, in submit order, which is the same on every rank.
 // ---------------------------------------------------------------------------
 struct spmvb_dist_pipeline_st {
-  spmvb_dist D = nullptr;
+  spmvb_dist D = nullptr;  // null once the dist handle was destroyed first
+  int device = 0;
   struct Slot {
     cudaStream_t stream = nullptr;
     cudaEvent_t copied = nullptr, gathered = nullptr, done = nullptr;
@@ -717,6 +725,17 @@ struct spmvb_dist_pipeline_st {
   }
 };
 
+// The dist handle goes first: let the pipeline's work finish (its kernels
+// read the handle's matrix and its all-gathers use the handle's
+// communicator), then make its later calls fail.
+static void detach_pipeline(spmvb_dist_pipeline_st* P) {
+  if (P->comm) cudaStreamSynchronize(P->comm);
+  for (auto& s : P->slots)
+    if (s.stream) cudaStreamSynchronize(s.stream);
+  P->D = nullptr;
+}
+
+
 extern "C" {
 
 spmvb_status spmvb_dist_pipeline_create(spmvb_dist D, int depth, spmvb_dist_pipeline* out) {
@@ -728,6 +747,7 @@ spmvb_status spmvb_dist_pipeline_create(spmvb_dist D, int depth, spmvb_dist_pipe
   DeviceGuard g(D->ctx->device);
   auto P = std::make_unique<spmvb_dist_pipeline_st>();
   P->D = D;
+  P->device = D->ctx->device;
   P->slots.resize(depth);
   const size_t es = dtype_size(D->dtype);
   SPMVB_TRY_CUDA(cudaStreamCreateWithFlags(&P->comm, cudaStreamNonBlocking));
@@ -739,14 +759,18 @@ spmvb_status spmvb_dist_pipeline_create(spmvb_dist D, int depth, spmvb_dist_pipe
     SPMVB_TRY(s.x.alloc(size_t(std::max(D->nranks * D->max_rows, 1)) * es));
     SPMVB_TRY(s.y.alloc(size_t(std::max(D->max_rows, 1)) * es));
   }
+  D->pipelines.push_back(P.get());
   *out = P.release();
   return SPMVB_OK;
 }
 
+static const char* kDetached = "the pipeline's dist handle was destroyed";
+
 spmvb_status spmvb_dist_pipeline_fork(spmvb_dist_pipeline P, void* stream) {
   clear_error();
   if (!P) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null pipeline");
-  DeviceGuard g(P->D->ctx->device);
+  if (!P->D) return fail(SPMVB_ERR_INVALID_ARGUMENT, kDetached);
+  DeviceGuard g(P->device);
   SPMVB_TRY_CUDA(cudaEventRecord(P->fork, static_cast<cudaStream_t>(stream)));
   SPMVB_TRY_CUDA(cudaStreamWaitEvent(P->comm, P->fork, 0));
   for (auto& s : P->slots) SPMVB_TRY_CUDA(cudaStreamWaitEvent(s.stream, P->fork, 0));
@@ -757,6 +781,7 @@ spmvb_status spmvb_dist_pipeline_submit(spmvb_dist_pipeline P, spmvb_kernel kern
                                         const void* h_x_local, void* h_y_local) {
   clear_error();
   if (!P) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null pipeline");
+  if (!P->D) return fail(SPMVB_ERR_INVALID_ARGUMENT, kDetached);
   spmvb_dist D = P->D;
   const int32_t rows = D->bounds[D->rank + 1] - D->bounds[D->rank];
   if (rows && (!h_x_local || !h_y_local)) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null host buffer");
@@ -769,9 +794,9 @@ spmvb_status spmvb_dist_pipeline_submit(spmvb_dist_pipeline P, spmvb_kernel kern
   unsigned char* mine = s.x.as<unsigned char>() + size_t(D->rank) * D->max_rows * es;
   if (rows) SPMVB_TRY_CUDA(cudaMemcpyAsync(mine, h_x_local, size_t(rows) * es, cudaMemcpyHostToDevice, s.stream));
   if (D->nranks > 1) {
-    const ncclDataType_t t = D->dtype == SPMVB_F64 ? ncclFloat64 : ncclFloat32;
     SPMVB_TRY_CUDA(cudaEventRecord(s.copied, s.stream));
     SPMVB_TRY_CUDA(cudaStreamWaitEvent(P->comm, s.copied, 0));
+    const ncclDataType_t t = D->dtype == SPMVB_F64 ? ncclFloat64 : ncclFloat32;
     SPMVB_TRY(nccl_enqueued(D->comm, ncclAllGather(mine, s.x.get(), size_t(D->max_rows), t, D->comm, P->comm),
                             "ncclAllGather(x slices)"));
     SPMVB_TRY_CUDA(cudaEventRecord(s.gathered, P->comm));
@@ -792,7 +817,8 @@ spmvb_status spmvb_dist_pipeline_submit(spmvb_dist_pipeline P, spmvb_kernel kern
 spmvb_status spmvb_dist_pipeline_join(spmvb_dist_pipeline P, void* stream) {
   clear_error();
   if (!P) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null pipeline");
-  DeviceGuard g(P->D->ctx->device);
+  if (!P->D) return fail(SPMVB_ERR_INVALID_ARGUMENT, kDetached);
+  DeviceGuard g(P->device);
   for (auto& s : P->slots)
     if (s.used) SPMVB_TRY_CUDA(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), s.done, 0));
   return SPMVB_OK;
@@ -801,7 +827,8 @@ spmvb_status spmvb_dist_pipeline_join(spmvb_dist_pipeline P, void* stream) {
 spmvb_status spmvb_dist_pipeline_wait(spmvb_dist_pipeline P) {
   clear_error();
   if (!P) return fail(SPMVB_ERR_INVALID_ARGUMENT, "null pipeline");
-  DeviceGuard g(P->D->ctx->device);
+  if (!P->D) return fail(SPMVB_ERR_INVALID_ARGUMENT, kDetached);
+  DeviceGuard g(P->device);
   SPMVB_TRY_CUDA(cudaStreamSynchronize(P->comm));
   for (auto& s : P->slots) SPMVB_TRY_CUDA(cudaStreamSynchronize(s.stream));
   return check_err_word(P->D->ctx, P->slots[0].stream);
@@ -810,7 +837,11 @@ spmvb_status spmvb_dist_pipeline_wait(spmvb_dist_pipeline P) {
 spmvb_status spmvb_dist_pipeline_destroy(spmvb_dist_pipeline P) {
   clear_error();
   if (!P) return SPMVB_OK;
-  DeviceGuard g(P->D->ctx->device);
+  DeviceGuard g(P->device);
+  if (P->D) {
+    auto& v = P->D->pipelines;
+    v.erase(std::remove(v.begin(), v.end(), P), v.end());
+  }
   delete P;
   return SPMVB_OK;
 }

@@ -160,6 +160,25 @@ def test_dist_pipeline_single_rank_matches_oracle(ctx, depth, kernel):
     D.close()
 
 
+def test_dist_pipeline_outlived_by_nothing(ctx):
+    """Destroying the dist handle before its host-buffer pipeline lets the
+    pipeline's calls in flight finish, after which the pipeline's calls fail
+    with an error (not a crash) and its destroy still succeeds."""
+    A = S.generate(2, seed=89, scale_rows=30000)
+    D = S.DistMatrix(ctx, 1, 0, None, A, S.partition_rows(A.rowptr, 1), S.F64)
+    P = S.DistPipeline(D, depth=2)
+    x = torch.from_numpy(S.generate_vector(90, A.n)).pin_memory()
+    y = torch.full((A.m,), float("nan"), dtype=torch.float64).pin_memory()
+    P.submit(x.numpy(), y.numpy(), kernel=S.ELL)
+    D.close()
+    assert_bitwise(oracle_y(A, x.numpy(), S.F64, S.F64), y.numpy(), "call finished before the handle went")
+    with pytest.raises(S.SpmvbError):
+        P.submit(x.numpy(), y.numpy(), kernel=S.ELL)
+    with pytest.raises(S.SpmvbError):
+        P.wait()
+    P.close()
+
+
 @pytest.mark.parametrize("depth", [1, 3])
 def test_pipeline_streams_host_buffers(ctx, depth):
     """Streamed host-buffer SpMV: 7 calls with different x and separate y
