@@ -609,7 +609,11 @@ def main():
     r0, r1 = int(bounds[rank]), int(bounds[rank + 1])
     B = row_block(S, A, r0, r1)
     block_bytes = kernel_bytes(S, kernel, None, B.m, B.n, B.nnz) if kernel != S.BCSR else None
-    copies = max(1, min(16, math.ceil(1.5 * gpu["l2_bytes"] / max(1, block_bytes or 1))))
+    # Copies of the block's matrix arrays (its bytes less x and y, which every
+    # copy shares or rewrites) such that 1.5x the L2 of them pass between two
+    # uses of a copy.
+    matrix_bytes = (block_bytes - 8 * (B.n + B.m)) if block_bytes else 0
+    copies = max(1, min(16, math.ceil(1.5 * gpu["l2_bytes"] / max(1, matrix_bytes))))
     mats = []
     for _ in range(copies):
         Mc = S.DeviceMatrix(ctx, B, S.F64)
