@@ -16,8 +16,10 @@
 namespace spmvb {
 
 constexpr int kRowThreads = 256;
-// Threads per CTA of ell_rows (see its launch).
+// Threads per CTA of ell_rows (see its launch): 64, or 32 for at most
+// kEllSmallRows rows.
 constexpr int kEllThreads = 64;
+constexpr int kEllSmallRows = 160000;
 // BCSR: blocks requested per batch per thread.
 constexpr int kBcsrBatch = 2;
 // Warp-staged scalar kernel: entries per warp chunk.
@@ -133,11 +135,13 @@ spmvb_status launch_spmv(spmvb_matrix A, spmvb_kernel kernel, int lanes,
         else if (stages == 4) SPMVB_TRY((launch_ell_tma<T, Acc, kEllTmaMaxWidth, 4>(A, e, x, y, stream)));
         else SPMVB_TRY((launch_ell_tma<T, Acc, kEllTmaMaxWidth, 3>(A, e, x, y, stream)));
       } else {
-        // 64-thread CTAs: a row block that fills less than one wave (an
-        // 8-way shard of 1M rows: 125k rows) spreads over the SMs within 2 %
-        // instead of the 21 % that 256-thread CTAs leave (measured 11.4 us
-        // against 12.6 us; no change at 1M rows).
-        ell_rows<T, Acc, false><<<(A->m + kEllThreads - 1) / kEllThreads, kEllThreads, 0, stream>>>(e, x, y);
+        // Small CTAs: a row block that fills less than one wave (an 8-way
+        // shard of 1M rows: 125k rows) spreads over the SMs within 2 % with
+        // 64-thread CTAs instead of the 21 % that 256-thread CTAs leave
+        // (11.4 against 12.6 us), and 32-thread CTAs gain 2 % more there
+        // (11.0 against 11.2 us); from 250k rows on 64 is 1 % faster.
+        const int threads = A->m <= kEllSmallRows ? 32 : kEllThreads;
+        ell_rows<T, Acc, false><<<(A->m + threads - 1) / threads, threads, 0, stream>>>(e, x, y);
       }
       count_launch();
       break;
