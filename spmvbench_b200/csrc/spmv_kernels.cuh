@@ -455,10 +455,10 @@ __global__ void __launch_bounds__(256)
 //    Deterministic, re-associated (bounded by 2*gamma_n*sum|a_ij x_j|).
 //
 // Remaining blocks: y = 0 for the empty rows when K = 0.
-template <typename T, typename Acc>
-__global__ void __launch_bounds__(256)
+template <typename T, typename Acc, int NT>
+__global__ void __launch_bounds__(NT)
     hyb_rows(HybView H, const T* __restrict__ x, Acc* __restrict__ y) {
-  constexpr int W = 256 / kWarp;
+  constexpr int W = NT / kWarp;
   constexpr int PER = kHybChunk / kWarp;
   __shared__ Acc s_prod[W][swz_size<Acc>(kHybChunk)];  // padded: conflict-free row sums
   const uint64_t ps = policy_evict_first();

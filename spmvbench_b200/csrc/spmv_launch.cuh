@@ -20,6 +20,10 @@ constexpr int kRowThreads = 256;
 // kEllSmallRows rows.
 constexpr int kEllThreads = 64;
 constexpr int kEllSmallRows = 160000;
+// Threads per CTA of hyb_rows: 4 chunk warps per CTA instead of 8, so a
+// CTA's slot frees as soon as fewer chunks are done: 32.7 against 33.9 us
+// fp64 on the power-law matrix (bit-identical), fp32 unchanged.
+constexpr int kHybThreads = 128;
 // BCSR: blocks requested per batch per thread.
 constexpr int kBcsrBatch = 2;
 // Warp-staged scalar kernel: entries per warp chunk.
@@ -173,12 +177,12 @@ spmvb_status launch_spmv(spmvb_matrix A, spmvb_kernel kernel, int lanes,
       h.n_chunks = A->hyb_n_chunks;
       h.n_split = A->hyb_n_split;
       h.n_empty = A->hyb_n_empty;
-      h.ell_blocks = A->hyb_K > 0 ? (A->m + kRowThreads - 1) / kRowThreads : 0;
-      h.chunk_blocks = (h.n_chunks + kRowThreads / kWarp - 1) / (kRowThreads / kWarp);
-      const int empty_blocks = (h.n_empty + kRowThreads - 1) / kRowThreads;
+      h.ell_blocks = A->hyb_K > 0 ? (A->m + kHybThreads - 1) / kHybThreads : 0;
+      h.chunk_blocks = (h.n_chunks + kHybThreads / kWarp - 1) / (kHybThreads / kWarp);
+      const int empty_blocks = (h.n_empty + kHybThreads - 1) / kHybThreads;
       const int grid = h.ell_blocks + h.chunk_blocks + empty_blocks;
       if (grid > 0) {
-        hyb_rows<T, Acc><<<grid, kRowThreads, 0, stream>>>(h, x, y);
+        hyb_rows<T, Acc, kHybThreads><<<grid, kHybThreads, 0, stream>>>(h, x, y);
         count_launch();
       }
       break;
